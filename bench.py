@@ -1,0 +1,443 @@
+#!/usr/bin/env python
+"""Benchmark of the GLA hot path on B200 (one JSON line on rank 0).
+
+Headline workload: chunk_gla forward + backward at the
+GLA-1.3B layer shape B=8, T=4096, H=4, K=256, V=512, chunk 64, bf16 q/k/v/do,
+fp32 gates g = logsigmoid(N(0,1))/16, h0 = 0.  One step = fwd (saving what the
+backward needs) + bwd -> dq, dk, dv, dg.  Metric: tokens/s (B*T per step, summed
+over ranks).  The same line carries the decode step (
+fused_recurrent_gla, B=256, T=1, H=16, K=V=128, fp32 state) in HBM GB/s.
+
+Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
+batch x heads shard -- the units are independent, so there is no collective on
+the data path ("scaling": "weak"); timing is max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Inputs (537 MB per step) exceed the 126 MB L2, so no flush is needed between
+steps.  `--impl reference` times the CPU restatement of the reference algorithm
+(oracle/, float32 numpy, all host threads) on a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "pallas-kernel_b200"))
+
+METRIC = "chunk_gla fwd+bwd tokens/s (1-8 B200), % tensor peak; decode step HBM GB/s"
+CFG3 = dict(B=8, T=4096, H=4, K=256, V=512, C=64)
+CFG2 = dict(B=256, T=1, H=16, K=128, V=128)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm_gbs=float(d["hbm_gbs"]), bf16=float(d["bf16_tflops"]),
+                    bf16_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), source="measured")
+    return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
+
+
+# algorithmic work per token per head (dense C x C tiles, no recompute) -- per kernel
+def kernel_flops(name, K, V, C):
+    return {
+        "chunk_fwd_h": 2 * K * V, "chunk_fwd_intra": 2 * C * K, "chunk_fwd_o": 2 * K * V + 2 * C * V,
+        "chunk_bwd_dh": 2 * K * V, "chunk_bwd_dA": 2 * C * V, "chunk_bwd_dv": 2 * C * V + 2 * K * V,
+        "chunk_bwd_dqk_intra": 4 * C * K, "chunk_bwd_dqkg": 4 * K * V,
+        "tc_chunk_fwd": 4 * K * V + 2 * C * (K + V),
+        "tc_chunk_bwd_dh": 2 * K * V + 2 * C * V + 2 * K * V,
+        "tc_chunk_bwd_dqkg": 2 * C * V + 4 * C * K + 4 * K * V,
+    }.get(name)
+
+
+def fwd_bwd_flops_per_token_head(K, V, C):
+    return 12 * K * V + 6 * C * (K + V)
+
+
+def fwd_bwd_bytes_per_token_head(K, V):
+    # fwd: q,k (bf16) v (bf16) g (fp32) read, o (bf16) written;
+    # bwd: q,k,v,g,do read; dq,dk,dv (bf16), dg (fp32) written
+    fwd = 2 * K + 2 * K + 2 * V + 4 * K + 2 * V
+    bwd = 2 * K + 2 * K + 2 * V + 4 * K + 2 * V + 2 * K + 2 * K + 2 * V + 4 * K
+    return fwd + bwd
+
+
+class Clocks:
+    """nvidia-smi sampler during the timed region (clocks and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        self.out = ""
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.4)  # let the sampler start before the timed region
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), smax=float(f[2]), power=float(f[3]),
+                                 hw=f[5], hwt=f[6], swt=f[7], pcap=f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        load = [r for r in rows if r["power"] > 200] or rows
+        reasons = set()
+        for r in load:
+            for key, nm in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                            ("pcap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (numpy float32 restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+
+def cpu_sample(seconds_budget: float = 20.0, T: int = 1024):
+    import numpy as np
+
+    from oracle import gla_oracle as O
+    c = CFG3
+    rng = np.random.default_rng(0)
+    B, H, K, V, C = 1, c["H"], c["K"], c["V"], c["C"]
+    q, k = (rng.standard_normal((B, T, H, K), dtype=np.float32) for _ in range(2))
+    v = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    g = (-np.logaddexp(0, -rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    runs = []
+    t_end = time.perf_counter() + seconds_budget
+    while True:
+        t0 = time.perf_counter()
+        gc, A, h, _, o = O.chunk_gla_fwd(q, k, v, g, None, K ** -0.5, None, False, None, C, dtype=np.float32)
+        O.chunk_gla_bwd(q, k, v, g, gc, K ** -0.5, None, h, A, do, None, None, C, dtype=np.float32)
+        runs.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(runs) >= 3:
+            break
+    dt = statistics.median(runs)
+    return {"value": B * T / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle fwd+bwd, numpy float32 (BLAS threads = all host cores), 1 sequence x {T} tokens "
+                      f"x H={H} at K={K} V={V} C={C}; median of {len(runs)}"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import gla_oracle as O
+    c = CFG3
+    T = 1024
+    rng = np.random.default_rng(0)
+    H, K, V, C = c["H"], c["K"], c["V"], c["C"]
+    q, k = (rng.standard_normal((1, T, H, K), dtype=np.float32) for _ in range(2))
+    v = rng.standard_normal((1, T, H, V), dtype=np.float32)
+    g = (-np.logaddexp(0, -rng.standard_normal((1, T, H, K))) / 16).astype(np.float32)
+    do = rng.standard_normal((1, T, H, V), dtype=np.float32)
+
+    def step():
+        gc, A, h, _, o = O.chunk_gla_fwd(q, k, v, g, None, K ** -0.5, None, False, None, C, dtype=np.float32)
+        O.chunk_gla_bwd(q, k, v, g, gc, K ** -0.5, None, h, A, do, None, None, C, dtype=np.float32)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    val = T / dt
+    sample = (f"oracle (CPU restatement of the reference algorithm; JAX reference not installable), "
+              f"numpy float32, all host threads; each step = 1 sequence x {T} tokens x H={H} of config 3")
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "chunk_gla fwd+bwd, config 3 shape (B8 T4096 H4 K256 V512 C64), bounded sample",
+                       "sample_tokens_per_step": T},
+            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    del world
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def make_inputs(dev, seed):
+    import torch
+    c = CFG3
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    bf = torch.bfloat16
+    q = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
+    k = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    g = torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16
+    do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    return q, k, v, g.contiguous(), do
+
+
+def run_ours(args):
+    import torch
+
+    from tops import _C
+    from tops.ops.gla import _core
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    c = CFG3
+    B, T, H, K, V, C = c["B"], c["T"], c["H"], c["K"], c["V"], c["C"]
+    q, k, v, g, do = make_inputs(dev, 1234 + rank)
+    plan = _core.make_plan(q, V, C, None, K ** -0.5)
+
+    def step():
+        o, _, saved = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+        gc, A, h = saved
+        return _core.chunk_bwd(plan, q, k, v, g, None, do, None, gc, A, h, False)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier(world)
+    l0 = _C.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(local).__enter__()
+    barrier(world)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier(world)
+    launches = (_C.launch_count() - l0) // max(args.steps, 1)
+    ms = ev0.elapsed_time(ev1) / max(args.steps, 1)
+    ms = max_over_ranks(ms, world)
+    tokens = B * T * world
+    value = tokens / (ms * 1e-3)
+
+    # per-kernel live timing (CUDA events around each launch on its stream)
+    _C.timing_enable(True)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    _C.timing_enable(False)
+    rec = _C.timing_collect()
+    per = {}
+    for nm, t in rec:
+        d = per.setdefault(nm, [0.0, 0])
+        d[0] += t
+        d[1] += 1
+    tot = sum(v_[0] for v_ in per.values()) or 1.0
+    dom = max(per.items(), key=lambda kv: kv[1][0])
+    dom_name, (dom_total, dom_n) = dom
+    dom_ms = dom_total / dom_n
+    pk = peaks()
+    flops_tok = kernel_flops(dom_name, K, V, C)
+    units = B * T * H
+    kernels_share = {nm: round(v_[0] / tot, 4) for nm, v_ in sorted(per.items(), key=lambda kv: -kv[1][0])}
+    traffic = None
+    tj = ROOT / "profiles" / "traffic.json"
+    if tj.exists():
+        traffic = json.loads(tj.read_text()).get(dom_name)
+    roof = {"kernel": dom_name, "bound": "tensor", "unit": "TFLOP/s",
+            "achieved": (flops_tok * units / (dom_ms * 1e-3)) / 1e12 if flops_tok else None,
+            "peak": pk["bf16_sustained"], "peak_source": f"{pk['source']} bf16 sustained (kernel timed inside a step)",
+            "traffic": traffic, "kernel_ms": dom_ms, "kernel_shares": kernels_share}
+    roof["frac"] = roof["achieved"] / roof["peak"] if roof["achieved"] else None
+    step_flops = fwd_bwd_flops_per_token_head(K, V, C) * units
+    step_bytes = fwd_bwd_bytes_per_token_head(K, V) * units
+    step_roof = {"tflops": step_flops / (ms * 1e-3) / 1e12, "tensor_frac": step_flops / (ms * 1e-3) / 1e12 / pk["bf16"],
+                 "gbs": step_bytes / (ms * 1e-3) / 1e9, "hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                 "binding_roof_frac": max(step_flops / (pk["bf16"] * 1e12), step_bytes / (pk["hbm_gbs"] * 1e9))
+                 / (ms * 1e-3)}
+
+    # ---- decode step (config 2) -------------------------------------------------
+    dec = decode_bench(args, world, local, dev)
+
+    # ---- end to end through the public API with host buffers ---------------------
+    e2e = e2e_bench(args, world, dev, q, k, v, g, do, plan)
+    clk.__exit__()
+
+    clocks = clk.summary()
+    if rank == 0:
+        cpu = cpu_sample() if world == 1 else None
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "chunk_gla fwd+bwd (BASELINE config 3)", "B_per_gpu": B, "T": T, "H": H,
+                           "K": K, "V": V, "chunk_size": C, "global_batch": B * world,
+                           "parallelism": f"batch x heads shards, {world} GPU(s), no collective",
+                           "l2": "inputs (537 MB/step) larger than L2; no flush"},
+                "roofline": roof, "step_roofline": step_roof, "decode": dec, "e2e": e2e,
+                "gpu_launches": int(launches), "clocks": clocks, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def decode_bench(args, world, local, dev):
+    import torch
+
+    from tops.ops.gla import _core
+    c = CFG2
+    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    gen = torch.Generator(device=dev).manual_seed(7)
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    gk = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
+    h0 = torch.randn(B, H, K, V, device=dev, generator=gen) * 0.1
+    scale = K ** -0.5
+
+    def step():
+        return _core.recurrent_fwd(q, k, v, gk, None, h0, scale, True, False, None, B)
+
+    for _ in range(5):
+        step()
+    steps = max(args.steps, 20)
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    nbytes = 2 * B * H * K * V * 4 + B * T * H * (2 * K * 2 + 2 * V + 4 * K + 4 * V)
+    pk = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"metric": "fused_recurrent_gla decode step HBM GB/s (BASELINE config 2)", "value": gbs * world,
+            "unit": "GB/s", "per_gpu_gbs": gbs, "us_per_step": ms * 1e3, "bytes_per_step": nbytes,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"], "kernel": "recurrent_fwd"},
+            "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "state": "fp32", "inputs": "bf16 q/k/v, fp32 gk"}}
+
+
+def e2e_bench(args, world, dev, q, k, v, g, do, plan):
+    """Public C-ABI path with HOST buffers: H2D of q,k,v,g,do and D2H of dq,dk,dv,dg per step."""
+    import torch
+
+    from tops.ops.gla import _core
+    hq, hk, hv, hg, hdo = (x.cpu().pin_memory() for x in (q, k, v, g, do))
+    outs = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (q, k, v, g)]
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hg, hdo))
+    d2h = sum(x.numel() * x.element_size() for x in outs)
+
+    def step():
+        dq_, dk_, dv_, dg_ = (x.to(dev, non_blocking=True) for x in (hq, hk, hv, hg))
+        ddo = hdo.to(dev, non_blocking=True)
+        o, _, saved = _core.chunk_fwd(plan, dq_, dk_, dv_, dg_, None, False, save=True)
+        gc, A, h = saved
+        r = _core.chunk_bwd(plan, dq_, dk_, dv_, dg_, None, ddo, None, gc, A, h, False)
+        for dst, src in zip(outs, r[:4]):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    steps = max(3, min(args.steps, 10))
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    tokens = plan.B * plan.T * world
+    return {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "path": "tops.ops.gla C ABI (chunk fwd+bwd) with pinned host inputs/outputs"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,237 @@
+/*
+ * tops_gla.h -- C ABI of the B200-native Gated Linear Attention library (libtops_gla.so).
+ *
+ * This is the drop-in boundary for the GLA operators of the reference package
+ * `tops` (primatrix/pallas-kernel).  The reference has no FFI: its boundary is the
+ * Python module `tops.ops.gla` (tops/ops/gla/__init__.py:1-34) whose functions
+ * launch Pallas-TPU kernels in-process.  Each entry point below replaces one of
+ * those functions (cited per declaration); the Python package
+ * `pallas-kernel_b200/tops` binds them with ctypes and keeps the reference's
+ * Python signatures, and a JAX custom-call binding targets the same symbols.
+ *
+ * Conventions
+ *  - All tensor pointers are DEVICE pointers to dense row-major (contiguous)
+ *    arrays.  Layout is [B, T, H, D] for token tensors (FLA convention) and
+ *    [N, H, K, V] for recurrent states; per-chunk states are [NT, H, K, V] with
+ *    chunks in sequence order (== the reference's [B, NT, H, K, V] or, for
+ *    variable-length input, [1, NT_total, H, K, V]).
+ *  - `dtype` is the storage type of q, k, v, o, do, dq, dk, dv (TOPS_F32, TOPS_BF16
+ *    or TOPS_F16).  Gates g/gk/gv, their gradients, states (h0, ht, dht, dh0) and
+ *    every per-chunk intermediate (g_cumsum, A, h, dh, dA) are fp32, as in the
+ *    reference (tops/ops/gla/chunk.py:1226-1231 casts to fp32;
+ *    tops/ops/gla/fused_recurrent.py:261-263 returns fp32 o/ht).
+ *  - Variable-length input: B == 1, `cu_seqlens` = device int32 [N+1] and
+ *    `chunk_offsets` = device int32 [N+1] from tops_gla_num_chunks() (the
+ *    reference computes the same map on the host: tops/utils.py:70-89).
+ *    Segments need not be multiples of chunk_size (ragged chunks behave as the
+ *    reference's per-segment zero padding, tops/ops/gla/chunk.py:751-793).
+ *  - Every function is stream-ordered on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream), allocates no device memory, and returns TOPS_OK (0) or a
+ *    negative status; tops_gla_last_error() gives the message (thread-local).
+ *    Nothing aborts, traps or waits without a bound.
+ */
+#ifndef TOPS_GLA_H_
+#define TOPS_GLA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TOPS_GLA_ABI_VERSION 1
+
+#if defined(__GNUC__) || defined(__clang__)
+#define TOPS_API __attribute__((visibility("default")))
+#else
+#define TOPS_API
+#endif
+
+enum tops_dtype { TOPS_F32 = 0, TOPS_BF16 = 1, TOPS_F16 = 2 };
+
+enum tops_status {
+  TOPS_OK = 0,
+  TOPS_ERR_INVALID = -1,      /* bad shape / null pointer / inconsistent arguments */
+  TOPS_ERR_UNSUPPORTED = -2,  /* valid request this build cannot serve (e.g. no sm_100 device) */
+  TOPS_ERR_CUDA = -3,         /* a CUDA runtime call failed */
+  TOPS_ERR_WORKSPACE = -4,    /* workspace missing or smaller than *_workspace_size() */
+  TOPS_ERR_TIMEOUT = -5       /* a bounded device-side wait gave up */
+};
+
+/* Problem description shared by every chunked entry point. */
+typedef struct tops_gla_shape {
+  int32_t B, T, H, K, V;       /* q,k: [B,T,H,K]  v: [B,T,H,V] */
+  int32_t N;                   /* number of sequences: B, or len(cu_seqlens)-1 */
+  int32_t NT;                  /* total chunks over all sequences (tops_gla_num_chunks) */
+  int32_t chunk_size;          /* power of two; the reference API default is 16 */
+  int32_t dtype;               /* enum tops_dtype of q/k/v/o/do/dq/dk/dv */
+  float scale;                 /* attention scale (reference default K^-0.5) */
+  const int32_t* cu_seqlens;   /* device [N+1] or NULL */
+  const int32_t* chunk_offsets;/* device [N+1] or NULL (required iff cu_seqlens) */
+} tops_gla_shape;
+
+/* ---- host helpers ------------------------------------------------------- */
+
+/* Number of chunks of a problem: B*ceil(T/C) or sum_n ceil(len_n/C) when
+ * `cu_seqlens_host` ([N+1], host memory) is given.  If `chunk_offsets_host` is not
+ * NULL it receives the [N+1] prefix (to be copied to the device by the caller).
+ * Replaces tops/utils.py:70-89 (prepare_chunk_indices).  Returns -1 on bad input. */
+TOPS_API int32_t tops_gla_num_chunks(int32_t B, int32_t T, int32_t chunk_size, const int32_t* cu_seqlens_host,
+                            int32_t N, int32_t* chunk_offsets_host);
+
+TOPS_API const char* tops_gla_last_error(void);
+/* Number of kernels (and device memsets) this library has launched in the process. */
+TOPS_API uint64_t tops_gla_launch_count(void);
+/* Per-launch timing for benchmarks: when enabled, every kernel launch is bracketed by
+ * CUDA events on its stream; tops_gla_timing_collect() waits for them, writes up to
+ * `max_entries` (name, milliseconds) pairs and clears the record.  Returns the number
+ * of launches recorded.  Off by default (no events, no overhead). */
+TOPS_API void tops_gla_timing_enable(int32_t on);
+TOPS_API int32_t tops_gla_timing_collect(char* names, int32_t name_stride, float* ms, int32_t max_entries);
+TOPS_API int32_t tops_gla_abi_version(void);
+/* 1 when the current device can run the tcgen05 (sm_100a) kernels. */
+TOPS_API int32_t tops_gla_has_tcgen05(void);
+
+/* ---- public operators ---------------------------------------------------- */
+
+typedef struct tops_gla_chunk_fwd_args {
+  tops_gla_shape s;
+  const void* q; const void* k; const void* v;
+  const float* g;              /* [B,T,H,K] log-space gates, NULL = no decay */
+  const float* h0;             /* [N,H,K,V] or NULL */
+  void* o;                     /* out [B,T,H,V] (dtype) */
+  float* ht;                   /* out [N,H,K,V] or NULL (output_final_state=False) */
+  /* Optional saved intermediates for the backward (reference chunk_gla_fwd
+   * returns (g_cumsum, A, h, ht, o), tops/ops/gla/chunk.py:1083-1179).  NULL = not
+   * returned.  Their layout follows `chunk_size`. */
+  float* g_cumsum;             /* [B,T,H,K] */
+  float* A;                    /* [B,T,H,C] */
+  float* h;                    /* [NT,H,K,V] */
+  void* workspace; size_t workspace_bytes;
+} tops_gla_chunk_fwd_args;
+
+/* Chunked GLA forward: o = chunk_gla(q,k,v,g,scale,h0)[0], ht = final state.
+ * Replaces tops.ops.gla.chunk_gla / chunk_gla_fwd (tops/ops/gla/chunk.py:1187,1083)
+ * and fused_chunk_gla (tops/ops/gla/fused_chunk.py:4). */
+TOPS_API int tops_gla_chunk_fwd(const tops_gla_chunk_fwd_args* a, void* stream);
+TOPS_API size_t tops_gla_chunk_fwd_workspace_size(const tops_gla_chunk_fwd_args* a);
+
+typedef struct tops_gla_chunk_bwd_args {
+  tops_gla_shape s;
+  const void* q; const void* k; const void* v;
+  const float* g;              /* raw gates or NULL */
+  const float* h0;             /* [N,H,K,V] or NULL */
+  const void* do_;             /* [B,T,H,V] (dtype) */
+  const float* dht;            /* [N,H,K,V] or NULL */
+  const float* g_cumsum;       /* optional saved fwd intermediates (NULL = recompute) */
+  const float* A;
+  const float* h;
+  void* dq; void* dk; void* dv;/* out (dtype) */
+  float* dg;                   /* out [B,T,H,K] fp32 */
+  float* dh0;                  /* out [N,H,K,V] or NULL */
+  void* workspace; size_t workspace_bytes;
+} tops_gla_chunk_bwd_args;
+
+/* Chunked GLA backward -> dq, dk, dv, dg, dh0.
+ * Replaces tops.ops.gla.chunk_gla_bwd (tops/ops/gla/chunk.py:815) and
+ * chunk_gla_bwd_with_pl (tops/ops/gla/chunk.py:980). */
+TOPS_API int tops_gla_chunk_bwd(const tops_gla_chunk_bwd_args* a, void* stream);
+TOPS_API size_t tops_gla_chunk_bwd_workspace_size(const tops_gla_chunk_bwd_args* a);
+
+typedef struct tops_gla_recurrent_args {
+  int32_t B, T, H, K, V, N;
+  int32_t dtype;               /* storage type of q, k, v */
+  float scale;
+  int32_t reverse;             /* iterate t = T-1 .. 0 */
+  const int32_t* cu_seqlens;   /* device [N+1] or NULL (then N == B) */
+  const void* q; const void* k; const void* v;
+  const float* gk;             /* [B,T,H,K] or NULL */
+  const float* gv;             /* [B,T,H,V] or NULL */
+  const float* h0;             /* [N,H,K,V] or NULL */
+  float* o;                    /* out [B,T,H,V] fp32 */
+  float* ht;                   /* out [N,H,K,V] or NULL */
+  void* workspace; size_t workspace_bytes;
+} tops_gla_recurrent_args;
+
+/* Token-by-token recurrence (decode).  Replaces tops.ops.gla.fused_recurrent_gla
+ * (tops/ops/gla/fused_recurrent.py:438 -> :379 -> :235, kernel :139). */
+TOPS_API int tops_gla_recurrent_fwd(const tops_gla_recurrent_args* a, void* stream);
+TOPS_API size_t tops_gla_recurrent_fwd_workspace_size(const tops_gla_recurrent_args* a);
+
+typedef struct tops_gla_recurrent_bwd_args {
+  tops_gla_recurrent_args f;   /* forward inputs (f.o / f.ht unused) */
+  const float* o;              /* forward output [B,T,H,V] fp32; required when f.gv is given
+                                  (as in the reference, fused_recurrent.py:934) */
+  const void* do_;             /* [B,T,H,V] (dtype) */
+  const float* dht;            /* [N,H,K,V] or NULL */
+  float* dq; float* dk; float* dv;   /* out fp32 */
+  float* dgk;                  /* out [B,T,H,K] or NULL (needs gk) */
+  float* dgv;                  /* out [B,T,H,V] or NULL (needs gv) */
+  float* dh0;                  /* out [N,H,K,V] or NULL */
+} tops_gla_recurrent_bwd_args;
+
+/* Backward of the recurrence.  Replaces tops.ops.gla.fused_recurrent_gla_bwd
+ * (tops/ops/gla/fused_recurrent.py:879; kernel :495; gate grads :798-876). */
+TOPS_API int tops_gla_recurrent_bwd(const tops_gla_recurrent_bwd_args* a, void* stream);
+TOPS_API size_t tops_gla_recurrent_bwd_workspace_size(const tops_gla_recurrent_bwd_args* a);
+
+/* ---- chunk sub-functions (exported by tops.ops.gla, __init__.py:2-14) ------ */
+
+/* g_cumsum = scale * chunk-local inclusive cumsum of g (suffix sums when reverse != 0).
+ * tops/ops/gla/chunk.py:110 (chunk_local_cumsum_vector; kernel :55). */
+TOPS_API int tops_gla_chunk_local_cumsum(const tops_gla_shape* s, const float* g, float* g_cumsum, int32_t reverse,
+                                         float scale, void* stream);
+
+/* h[c] = state at the start of chunk c; ht = final state.  tops/ops/common/chunk_h.py:137,277. */
+TOPS_API int tops_gla_chunk_fwd_h(const tops_gla_shape* s, const void* k, const void* v, const float* g_cumsum,
+                         const float* h0, float* h, float* ht, void* stream);
+
+/* Reverse scan: dh[c] = dL/d(state at the end of chunk c); dh0.  tops/ops/common/chunk_h.py:399,605. */
+TOPS_API int tops_gla_chunk_bwd_dh(const tops_gla_shape* s, const void* q, const float* g_cumsum, const void* do_,
+                          const float* dht, float* dh, float* dh0, void* stream);
+
+/* A = intra-chunk gated attention [B,T,H,C]; the full C x C block when causal == 0
+ * (as the exported reference sub-function returns it), lower-triangular when causal != 0
+ * (as chunk_gla_fwd uses it).  tops/ops/gla/chunk.py:386 (kernel :350, ref :300). */
+TOPS_API int tops_gla_chunk_fwd_intra(const tops_gla_shape* s, const void* q, const void* k, const float* g_cumsum,
+                                      int32_t causal, float* A, void* stream);
+
+/* o = scale (q e^G) h + tril(A) v.  tops/ops/gla/chunk.py:1387 (kernel :1259, ref :441). */
+TOPS_API int tops_gla_chunk_fwd_o(const tops_gla_shape* s, const void* q, const void* v, const float* g_cumsum,
+                         const float* A, const float* h, void* o, void* stream);
+
+/* dA = tril(scale do v^T).  tops/ops/gla/chunk.py:504 (chunk_gla_bwd_dA_ref). */
+TOPS_API int tops_gla_chunk_bwd_dA(const tops_gla_shape* s, const void* v, const void* do_, float* dA, void* stream);
+
+/* dv = tril(A)^T do + (k e^{G_last-G}) dh.  tops/ops/gla/chunk.py:547 (chunk_gla_bwd_dv_ref). */
+TOPS_API int tops_gla_chunk_bwd_dv(const tops_gla_shape* s, const void* k, const float* g_cumsum, const float* A,
+                          const void* do_, const float* dh, float* dv, void* stream);
+
+/* Intra-chunk dq, dk from dA.  tops/ops/gla/chunk.py:603 (chunk_gla_bwd_dqk_intra_ref). */
+TOPS_API int tops_gla_chunk_bwd_dqk_intra(const tops_gla_shape* s, const void* q, const void* k, const float* g_cumsum,
+                                 const float* dA, float* dq, float* dk, void* stream);
+
+/* Inter-chunk dq, dk (added to dq_in/dk_in) and dg.  tops/ops/gla/chunk.py:656 (chunk_gla_bwd_dqkg_ref).
+ * dq_out/dk_out have storage type `out_dtype` (enum tops_dtype); dg is fp32. */
+TOPS_API int tops_gla_chunk_bwd_dqkg(const tops_gla_shape* s, const void* q, const void* k, const void* v,
+                            const float* h, const float* g_cumsum, const void* do_, const float* dh,
+                            const float* dq_in, const float* dk_in, void* dq_out, void* dk_out,
+                            int32_t out_dtype, float* dg, void* stream);
+
+/* ---- sequence-parallel state hand-off (no reference counterpart: the reference
+ *      has no multi-device code; BASELINE config 4 asks for it) ------------- */
+
+/* D[n,h,k] = exp(sum over the sequence of g[.,h,k]): the total decay of a span. */
+TOPS_API int tops_gla_span_decay(const tops_gla_shape* s, const float* g, float* decay, void* stream);
+
+/* out = decay (broadcast over V) * h_in + s_local, all [N,H,K,V] fp32 (decay [N,H,K]).
+ * out may alias s_local. */
+TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, const float* decay, const float* h_in,
+                           const float* s_local, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOPS_GLA_H_ */

@@ -1,0 +1,260 @@
+"""Tensor-level wrappers of the libtops_gla C ABI (torch CUDA tensors in, out).
+
+Everything here is plumbing: shape checks, output allocation, the varlen chunk
+map (computed on the host exactly like the reference's ``prepare_chunk_indices``,
+``tops/utils.py:70-89``) and one C call per operation on the current CUDA stream.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ... import _C
+
+
+def _cuda(name: str, t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the GLA ops run only on the GPU), got {t.device}")
+    return t.contiguous()
+
+
+def _f32(name: str, t: torch.Tensor | None) -> torch.Tensor | None:
+    t = _cuda(name, t)
+    return None if t is None else t.float().contiguous()
+
+
+@dataclass
+class Plan:
+    """Problem geometry shared by the chunked entry points."""
+    B: int
+    T: int
+    H: int
+    K: int
+    V: int
+    N: int
+    NT: int
+    C: int
+    dtype: torch.dtype
+    scale: float
+    cu_host: list | None
+    cu_dev: torch.Tensor | None
+    offs_dev: torch.Tensor | None
+
+    def shape(self) -> _C.Shape:
+        return _C.Shape(self.B, self.T, self.H, self.K, self.V, self.N, self.NT, self.C, _C.dtype_code(self.dtype),
+                        float(self.scale), _C.ptr(self.cu_dev), _C.ptr(self.offs_dev))
+
+    @property
+    def nchunk_per_seq(self) -> int:
+        return (self.T + self.C - 1) // self.C
+
+
+def host_cu(cu_seqlens) -> list | None:
+    if cu_seqlens is None:
+        return None
+    if isinstance(cu_seqlens, torch.Tensor):
+        return [int(x) for x in cu_seqlens.detach().cpu().tolist()]
+    return [int(x) for x in cu_seqlens]
+
+
+def make_plan(q: torch.Tensor, V: int, chunk_size: int, cu_seqlens, scale: float | None) -> Plan:
+    B, T, H, K = q.shape
+    C = int(chunk_size)
+    assert C > 0 and (C & (C - 1)) == 0, f"chunk_size must be a power of 2, got {C}"
+    cu = host_cu(cu_seqlens)
+    if cu is None:
+        N, NT, cu_dev, offs_dev = B, B * ((T + C - 1) // C), None, None
+    else:
+        assert B == 1, f"Batch size must be 1 when using cu_seqlens, got {B}"
+        assert len(cu) >= 2 and cu[0] == 0 and cu[-1] == T, f"cu_seqlens must run from 0 to T={T}, got {cu}"
+        assert all(b >= a for a, b in zip(cu, cu[1:])), "cu_seqlens must be non-decreasing"
+        N = len(cu) - 1
+        offs = [0]
+        for a, b in zip(cu, cu[1:]):
+            offs.append(offs[-1] + (b - a + C - 1) // C)
+        NT = offs[-1]
+        cu_dev = torch.tensor(cu, dtype=torch.int32, device=q.device)
+        offs_dev = torch.tensor(offs, dtype=torch.int32, device=q.device)
+    if scale is None:
+        scale = K ** -0.5
+    return Plan(B, T, H, K, V, N, NT, C, q.dtype, float(scale), cu, cu_dev, offs_dev)
+
+
+def _ws(nbytes: int, dev) -> torch.Tensor | None:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=dev) if nbytes else None
+
+
+# ---------------------------------------------------------------------------
+# fused forward / backward
+# ---------------------------------------------------------------------------
+
+def chunk_fwd(p: Plan, q, k, v, g, h0, output_final_state: bool, save: bool):
+    """-> o, ht|None, (g_cumsum, A, h) when ``save`` else None."""
+    dev = q.device
+    o = torch.empty(p.B, p.T, p.H, p.V, dtype=q.dtype, device=dev)
+    ht = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if output_final_state else None
+    gc = A = h = None
+    if save:
+        gc = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
+        A = torch.empty(p.B, p.T, p.H, p.C, dtype=torch.float32, device=dev)
+        h = torch.empty(p.NT, p.H, p.K, p.V, dtype=torch.float32, device=dev)
+    a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(o), _C.ptr(ht),
+                        _C.ptr(gc), _C.ptr(A), _C.ptr(h), None, 0)
+    ws = _ws(_C.lib().tops_gla_chunk_fwd_workspace_size(a), dev)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_chunk_fwd", a, _C.stream_of(q))
+    return o, ht, ((gc, A, h) if save else None)
+
+
+def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh0: bool = False):
+    dev = q.device
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dg = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
+    dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_dh0 else None
+    a = _C.ChunkBwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(do), _C.ptr(dht),
+                        _C.ptr(gc), _C.ptr(A), _C.ptr(h), _C.ptr(dq), _C.ptr(dk), _C.ptr(dv), _C.ptr(dg),
+                        _C.ptr(dh0), None, 0)
+    ws = _ws(_C.lib().tops_gla_chunk_bwd_workspace_size(a), dev)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_chunk_bwd", a, _C.stream_of(q))
+    return dq, dk, dv, dg, dh0
+
+
+# ---------------------------------------------------------------------------
+# sub-functions
+# ---------------------------------------------------------------------------
+
+def cumsum(p: Plan, g, reverse=False, scale=1.0):
+    out = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=g.device)
+    s = p.shape()
+    _C.call("tops_gla_chunk_local_cumsum", s, _C.ptr(g), _C.ptr(out), int(bool(reverse)), float(scale),
+            _C.stream_of(g))
+    return out
+
+
+def fwd_h(p: Plan, k, v, gc, h0, want_h=True, want_ht=True):
+    dev = k.device
+    h = torch.empty(p.NT, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_h else None
+    ht = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_ht else None
+    _C.call("tops_gla_chunk_fwd_h", p.shape(), _C.ptr(k), _C.ptr(v), _C.ptr(gc), _C.ptr(h0), _C.ptr(h), _C.ptr(ht),
+            _C.stream_of(k))
+    return h, ht
+
+
+def bwd_dh(p: Plan, q, gc, do, dht, want_dh0):
+    dev = q.device
+    dh = torch.empty(p.NT, p.H, p.K, p.V, dtype=torch.float32, device=dev)
+    dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_dh0 else None
+    _C.call("tops_gla_chunk_bwd_dh", p.shape(), _C.ptr(q), _C.ptr(gc), _C.ptr(do), _C.ptr(dht), _C.ptr(dh),
+            _C.ptr(dh0), _C.stream_of(q))
+    return dh, dh0
+
+
+def intra(p: Plan, q, k, gc, causal: bool):
+    A = torch.empty(p.B, p.T, p.H, p.C, dtype=torch.float32, device=q.device)
+    _C.call("tops_gla_chunk_fwd_intra", p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(gc), int(bool(causal)), _C.ptr(A),
+            _C.stream_of(q))
+    return A
+
+
+def fwd_o(p: Plan, q, v, gc, A, h):
+    o = torch.empty(p.B, p.T, p.H, p.V, dtype=q.dtype, device=q.device)
+    _C.call("tops_gla_chunk_fwd_o", p.shape(), _C.ptr(q), _C.ptr(v), _C.ptr(gc), _C.ptr(A), _C.ptr(h), _C.ptr(o),
+            _C.stream_of(q))
+    return o
+
+
+def bwd_dA(p: Plan, v, do):
+    dA = torch.empty(p.B, p.T, p.H, p.C, dtype=torch.float32, device=v.device)
+    _C.call("tops_gla_chunk_bwd_dA", p.shape(), _C.ptr(v), _C.ptr(do), _C.ptr(dA), _C.stream_of(v))
+    return dA
+
+
+def bwd_dv(p: Plan, k, gc, A, do, dh):
+    dv = torch.empty(p.B, p.T, p.H, p.V, dtype=torch.float32, device=k.device)
+    _C.call("tops_gla_chunk_bwd_dv", p.shape(), _C.ptr(k), _C.ptr(gc), _C.ptr(A), _C.ptr(do), _C.ptr(dh), _C.ptr(dv),
+            _C.stream_of(k))
+    return dv
+
+
+def bwd_dqk_intra(p: Plan, q, k, gc, dA):
+    dq = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=q.device)
+    dk = torch.empty_like(dq)
+    _C.call("tops_gla_chunk_bwd_dqk_intra", p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(gc), _C.ptr(dA), _C.ptr(dq),
+            _C.ptr(dk), _C.stream_of(q))
+    return dq, dk
+
+
+def bwd_dqkg(p: Plan, q, k, v, h, gc, do, dh, dq_in, dk_in, out_dtype=torch.float32):
+    dq = torch.empty(p.B, p.T, p.H, p.K, dtype=out_dtype, device=q.device)
+    dk = torch.empty_like(dq)
+    dg = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=q.device)
+    _C.call("tops_gla_chunk_bwd_dqkg", p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(h), _C.ptr(gc), _C.ptr(do),
+            _C.ptr(dh), _C.ptr(dq_in), _C.ptr(dk_in), _C.ptr(dq), _C.ptr(dk), _C.dtype_code(out_dtype), _C.ptr(dg),
+            _C.stream_of(q))
+    return dq, dk, dg
+
+
+def span_decay(p: Plan, g):
+    d = torch.empty(p.N, p.H, p.K, dtype=torch.float32, device=g.device)
+    _C.call("tops_gla_span_decay", p.shape(), _C.ptr(g), _C.ptr(d), _C.stream_of(g))
+    return d
+
+
+def state_combine(decay, h_in, s_local, out=None):
+    N, H, K, V = s_local.shape
+    out = torch.empty_like(s_local) if out is None else out
+    _C.call("tops_gla_state_combine", N, H, K, V, _C.ptr(decay), _C.ptr(h_in), _C.ptr(s_local), _C.ptr(out),
+            _C.stream_of(s_local))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# recurrent
+# ---------------------------------------------------------------------------
+
+def _rec_args(q, k, v, gk, gv, h0, scale, reverse, cu_dev, N, o=None, ht=None):
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    return _C.RecArgs(B, T, H, K, V, N, _C.dtype_code(q.dtype), float(scale), int(bool(reverse)), _C.ptr(cu_dev),
+                      _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(gk), _C.ptr(gv), _C.ptr(h0), _C.ptr(o), _C.ptr(ht),
+                      None, 0)
+
+
+def recurrent_fwd(q, k, v, gk, gv, h0, scale, output_final_state, reverse, cu_dev, N):
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    dev = q.device
+    o = (torch.zeros if cu_dev is not None else torch.empty)(B, T, H, V, dtype=torch.float32, device=dev)
+    ht = torch.empty(N, H, K, V, dtype=torch.float32, device=dev) if output_final_state else None
+    a = _rec_args(q, k, v, gk, gv, h0, scale, reverse, cu_dev, N, o, ht)
+    ws = _ws(_C.lib().tops_gla_recurrent_fwd_workspace_size(a), dev)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_recurrent_fwd", a, _C.stream_of(q))
+    return o, ht
+
+
+def recurrent_bwd(q, k, v, gk, gv, h0, o, do, dht, scale, reverse, cu_dev, N):
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    dev = q.device
+    z = torch.zeros if cu_dev is not None else torch.empty
+    dq = z(B, T, H, K, dtype=torch.float32, device=dev)
+    dk = z(B, T, H, K, dtype=torch.float32, device=dev)
+    dv = z(B, T, H, V, dtype=torch.float32, device=dev)
+    dgk = z(B, T, H, K, dtype=torch.float32, device=dev) if gk is not None else None
+    dgv = z(B, T, H, V, dtype=torch.float32, device=dev) if gv is not None else None
+    dh0 = torch.empty(N, H, K, V, dtype=torch.float32, device=dev) if h0 is not None else None
+    f = _rec_args(q, k, v, gk, gv, h0, scale, reverse, cu_dev, N)
+    a = _C.RecBwdArgs(f, _C.ptr(o), _C.ptr(do), _C.ptr(dht), _C.ptr(dq), _C.ptr(dk), _C.ptr(dv), _C.ptr(dgk),
+                      _C.ptr(dgv), _C.ptr(dh0))
+    ws = _ws(_C.lib().tops_gla_recurrent_bwd_workspace_size(a), dev)
+    a.f.workspace, a.f.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_recurrent_bwd", a, _C.stream_of(q))
+    return dq, dk, dv, dgk, dgv, dh0
+

@@ -133,6 +133,8 @@ def rec_inputs(c):
         h0 = (rng.standard_normal((N, H, K, V), dtype=np.float32) * c["h0s"]).astype(np.float32)
     dht = rng.standard_normal((N, H, K, V), dtype=np.float32) if c.get("dht") else None
     do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    if c.get("bf16"):
+        do = bf16_round(do)
     return dict(q=q, k=k, v=v, gk=gk, gv=gv, h0=h0, dht=dht, do=do, cu=cu,
                 scale=c.get("scale", K ** -0.5), reverse=bool(c.get("reverse", False)))
 

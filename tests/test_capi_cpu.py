@@ -1,0 +1,106 @@
+"""CPU checks of the C-ABI library: it builds, loads without a GPU, exports every
+symbol declared in include/tops_gla.h, its struct layouts match the ctypes mirror,
+and argument validation rejects bad calls before touching the device."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tops_gla.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    sys.path.insert(0, str(ROOT / "pallas-kernel_b200"))
+    import build as B  # pallas-kernel_b200/build.py (incremental)
+    B.build()
+    from tops import _C
+    return _C
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"TOPS_API\s+[\w\s\*]+?\b(tops_gla_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_reference_ops():
+    syms = declared_symbols()
+    for need in ("tops_gla_chunk_fwd", "tops_gla_chunk_bwd", "tops_gla_recurrent_fwd", "tops_gla_recurrent_bwd",
+                 "tops_gla_chunk_fwd_h", "tops_gla_chunk_bwd_dh", "tops_gla_state_combine"):
+        assert need in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    so = ctypes.CDLL(str(lib.LIB_PATH))
+    missing = [s for s in declared_symbols() if not hasattr(so, s)]
+    assert not missing, f"not exported: {missing}"
+    assert set(declared_symbols()) == set(lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_struct_layouts_match_ctypes(lib, tmp_path):
+    """Compile a C probe against the header and compare sizeof/offsetof with ctypes."""
+    structs = {"tops_gla_shape": lib.Shape, "tops_gla_chunk_fwd_args": lib.ChunkFwdArgs,
+               "tops_gla_chunk_bwd_args": lib.ChunkBwdArgs, "tops_gla_recurrent_args": lib.RecArgs,
+               "tops_gla_recurrent_bwd_args": lib.RecBwdArgs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0;}")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {}
+    for line in out:
+        if line.strip():
+            c, f, n = line.split()
+            got[(c, f)] = int(n)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
+
+
+def test_num_chunks_matches_host_plan(lib):
+    L = lib.lib()
+    assert L.tops_gla_num_chunks(3, 37, 16, None, 3, None) == 9
+    cu = (ctypes.c_int32 * 4)(0, 13, 37, 50)
+    offs = (ctypes.c_int32 * 4)()
+    assert L.tops_gla_num_chunks(1, 50, 16, ctypes.cast(cu, ctypes.c_void_p), 3, ctypes.cast(offs, ctypes.c_void_p)) == 4
+    assert list(offs) == [0, 1, 3, 4]
+    bad = (ctypes.c_int32 * 3)(0, 10, 5)
+    assert L.tops_gla_num_chunks(1, 10, 16, ctypes.cast(bad, ctypes.c_void_p), 2, None) == -1
+
+
+def test_validation_rejects_bad_calls_without_a_device(lib):
+    L = lib.lib()
+    s = lib.Shape(2, 32, 4, 32, 64, 2, 4, 16, lib.BF16, 0.1, None, None)
+    a = lib.ChunkFwdArgs(s, None, None, None, None, None, None, None, None, None, None, None, 0)
+    assert L.tops_gla_chunk_fwd(ctypes.byref(a), None) == -1  # q/k/v/o missing
+    assert b"required" in L.tops_gla_last_error()
+    s2 = lib.Shape(2, 32, 4, 32, 64, 2, 4, 12, lib.BF16, 0.1, None, None)  # chunk 12 not a power of 2
+    assert L.tops_gla_chunk_local_cumsum(ctypes.byref(s2), 1, 1, 0, 1.0, None) == -1
+    s3 = lib.Shape(2, 32, 4, 32, 64, 2, 5, 16, lib.BF16, 0.1, None, None)  # wrong NT
+    assert L.tops_gla_chunk_fwd_h(ctypes.byref(s3), 1, 1, 1, None, 1, None, None) == -1
+    r = lib.RecArgs(2, 1, 4, 32, 64, 3, lib.BF16, 0.1, 0, None, 1, 1, 1, None, None, None, 1, None, None, 0)
+    assert L.tops_gla_recurrent_fwd(ctypes.byref(r), None) == -1  # N != B without cu_seqlens
+    assert L.tops_gla_abi_version() == 1
+
+
+def test_workspace_queries_are_pure(lib):
+    L = lib.lib()
+    s = lib.Shape(8, 4096, 4, 256, 512, 8, 8 * 64, 64, lib.BF16, 0.0625, None, None)
+    a = lib.ChunkFwdArgs(s, None, None, None, None, None, None, None, None, None, None, None, 0)
+    n = L.tops_gla_chunk_fwd_workspace_size(ctypes.byref(a))
+    assert n >= 8 * 4096 * 4 * (256 + 64) * 4  # g_cumsum + A (fp32) at least
+    b = lib.ChunkBwdArgs(s, *([None] * 15), None, 0)
+    assert L.tops_gla_chunk_bwd_workspace_size(ctypes.byref(b)) > n

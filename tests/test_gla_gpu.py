@@ -1,0 +1,327 @@
+"""Parity of the CUDA GLA ops (called through the C ABI via tops.ops.gla) with the
+reference's outputs (golden fixtures) and the numpy oracle.
+
+Tolerances (from the task's north star):
+  * fp32 inputs: max-abs/rel 1e-4 against the reference (|err| <= 1e-4 + 1e-4 |ref|);
+  * bf16 inputs: relative L2 <= 2e-2 against an fp32/fp64 reference of the same inputs.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import cases as GC
+from _util import assert_close, assert_rel_l2
+from oracle import gla_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FP32 = dict(atol=1e-4, rtol=1e-4)
+BF16_L2 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def gla():
+    import tops.ops.gla as G
+    from tops import _C
+    _C.lib()
+    return G
+
+
+def dev(x, dtype=torch.float32):
+    return None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to("cuda", dtype)
+
+
+# ---------------------------------------------------------------------------
+# chunk_gla forward/backward against the reference's fixtures (fp32)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", GC.CHUNK_CASES, ids=lambda c: c["name"])
+def test_chunk_fwd_bwd_matches_reference(gla, case):
+    c, inp, fx = GC.load("chunk", case["name"])
+    q, k, v, g = (dev(inp[n]) for n in "qkvg")
+    h0 = dev(inp["h0"])
+    gc, A, h, ht, o = gla.chunk_gla_fwd(q, k, v, g, None, None, inp["scale"], h0, True, cu_seqlens=inp["cu"],
+                                        chunk_size=inp["C"])
+    assert_close("o", o, fx["o"], **FP32)
+    assert_close("ht", ht, fx["ht"], **FP32)
+    if "h" in fx:
+        assert_close("g_cumsum", gc, fx["g_cumsum"], **FP32)
+        assert_close("A", A, fx["A"], **FP32)
+        assert_close("h", h, fx["h"], **FP32)
+    if "dq" not in fx:
+        return
+    dq, dk, dv, dg, dh0 = gla.chunk_gla_bwd(q, k, v, g, None, None, inp["scale"], h0, None, None, dev(inp["do"]),
+                                            dev(inp["dht"]), cu_seqlens=inp["cu"], chunk_size=inp["C"])
+    for nm, got in (("dq", dq), ("dk", dk), ("dv", dv), ("dg", dg)):
+        assert_close(nm, got, fx[nm], **FP32)
+    assert (dh0 is None) == ("dh0" not in fx)
+    if dh0 is not None:
+        assert_close("dh0", dh0, fx["dh0"], **FP32)
+
+
+@pytest.mark.parametrize("case", [c for c in GC.CHUNK_CASES if not c.get("fwd_only")][:12],
+                         ids=lambda c: c["name"])
+def test_chunk_gla_autograd_matches_reference(gla, case):
+    """The public op, differentiated by torch.autograd, gives the reference's gradients."""
+    c, inp, fx = GC.load("chunk", case["name"])
+    q, k, v, g = (dev(inp[n]).requires_grad_() for n in "qkvg")
+    h0 = dev(inp["h0"])
+    if h0 is not None:
+        h0.requires_grad_()
+    o, ht = gla.chunk_gla(q, k, v, g, scale=inp["scale"], initial_state=h0, output_final_state=True,
+                          cu_seqlens=inp["cu"], chunk_size=inp["C"])
+    assert_close("o", o, fx["o"], **FP32)
+    loss = (o * dev(inp["do"])).sum()
+    if inp["dht"] is not None:
+        loss = loss + (ht * dev(inp["dht"])).sum()
+    loss.backward()
+    for nm, t in (("dq", q), ("dk", k), ("dv", v), ("dg", g)):
+        assert_close(nm, t.grad, fx[nm], **FP32)
+    if h0 is not None and "dh0" in fx:
+        assert_close("dh0", h0.grad, fx["dh0"], **FP32)
+
+
+def test_cfg1_forward(gla):
+    """B2 T256 H4 K64 V64 C64 fp32, g = logsigmoid/16, h0 = 0, final state."""
+    c, inp, fx = GC.load("chunk", "cfg1")
+    o, ht = gla.chunk_gla(dev(inp["q"]), dev(inp["k"]), dev(inp["v"]), dev(inp["g"]), scale=inp["scale"],
+                          initial_state=dev(inp["h0"]), output_final_state=True, chunk_size=64)
+    assert_close("o", o, fx["o"], **FP32)
+    assert_close("ht", ht, fx["ht"], **FP32)
+
+
+# ---------------------------------------------------------------------------
+# bf16 inputs: rel-L2 2e-2 against the fp64 oracle on the same (bf16-valued) inputs
+# ---------------------------------------------------------------------------
+
+BF16_CASES = [
+    dict(B=2, T=256, H=4, K=64, V=64, C=64, seed=1),
+    dict(B=1, T=300, H=2, K=128, V=256, C=64, seed=2, h0=True, dht=True),
+    dict(B=1, T=200, H=2, K=256, V=128, C=64, seed=3, cu=[0, 50, 130, 200]),
+    dict(B=2, T=128, H=2, K=32, V=48, C=16, seed=4),
+]
+
+
+@pytest.mark.parametrize("case", BF16_CASES, ids=lambda c: f"B{c['B']}T{c['T']}K{c['K']}V{c['V']}C{c['C']}")
+def test_chunk_bf16_fwd_bwd_vs_oracle(gla, case):
+    rng = np.random.default_rng(case["seed"])
+    B, T, H, K, V = case["B"], case["T"], case["H"], case["K"], case["V"]
+    N = len(case["cu"]) - 1 if case.get("cu") else B
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    do = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    h0 = rng.standard_normal((N, H, K, V), dtype=np.float32) if case.get("h0") else None
+    dht = rng.standard_normal((N, H, K, V), dtype=np.float32) if case.get("dht") else None
+    scale = K ** -0.5
+    o_r, ht_r = O.chunk_gla(q, k, v, g, scale=scale, initial_state=h0, output_final_state=True,
+                            cu_seqlens=case.get("cu"), chunk_size=case["C"])
+    dq_r, dk_r, dv_r, dg_r, dh0_r = O.chunk_gla_bwd(q, k, v, g, None, scale, h0, None, None, do, dht,
+                                                    case.get("cu"), case["C"])
+    bf = torch.bfloat16
+    qt, kt, vt = (dev(x, bf).requires_grad_() for x in (q, k, v))
+    gt = dev(g).requires_grad_()
+    h0t = dev(h0)
+    o, ht = gla.chunk_gla(qt, kt, vt, gt, scale=scale, initial_state=h0t, output_final_state=True,
+                          cu_seqlens=case.get("cu"), chunk_size=case["C"])
+    assert o.dtype == bf and ht.dtype == torch.float32
+    assert_rel_l2("o", o, o_r, BF16_L2)
+    assert_rel_l2("ht", ht, ht_r, BF16_L2)
+    loss = (o.float() * dev(do)).sum() + (0 if dht is None else (ht * dev(dht)).sum())
+    loss.backward()
+    for nm, got, want in (("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r), ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r)):
+        assert_rel_l2(nm, got, want, BF16_L2)
+
+
+# ---------------------------------------------------------------------------
+# sub-functions
+# ---------------------------------------------------------------------------
+
+def test_subfunctions_match_oracle(gla):
+    rng = np.random.default_rng(11)
+    B, T, H, K, V, C = 2, 100, 3, 40, 72, 32
+    q, k = rng.standard_normal((2, B, T, H, K), dtype=np.float32)
+    v = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    g = GC.logsigmoid(rng.standard_normal((B, T, H, K))).astype(np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    scale = 0.3
+    gc_r = O.chunk_local_cumsum(g, C)
+    gc = gla.chunk_local_cumsum(dev(g), C)
+    assert_close("cumsum", gc, gc_r, **FP32)
+    rev = gla.chunk_local_cumsum(dev(g), C, reverse=True, scale=2.0)
+    rev_r = np.zeros_like(g, dtype=np.float64)
+    for s in range(0, T, C):
+        e = min(s + C, T)
+        rev_r[:, s:e] = 2.0 * np.cumsum(g[:, s:e][:, ::-1], axis=1)[:, ::-1]
+    assert_close("cumsum_rev", rev, rev_r, **FP32)
+    h_r, ht_r = O.chunk_fwd_h(k, v, gc_r, h0, True, None, C)
+    h, ht = gla.chunk_fwd_h(dev(k), dev(v), dev(gc_r), dev(h0), True, chunk_size=C)
+    assert_close("h", h, h_r, **FP32)
+    assert_close("ht", ht, ht_r, **FP32)
+    A_full = gla.chunk_gla_fwd_intra_gk(dev(q), dev(k), dev(gc_r), scale, C)
+    A_r = O.chunk_gla_fwd_intra_gk(q, k, gc_r, scale, None, C)  # causal
+    tril = np.zeros_like(A_r)
+    for s in range(0, T, C):
+        L = min(C, T - s)
+        tril[:, s:s + L, :, :L] = np.tril(np.ones((L, L)))[:, None, :]
+    assert_close("A(lower)", A_full.cpu().numpy() * tril, A_r, **FP32)
+    o = gla.chunk_gla_fwd_o_gk(dev(q), dev(v), dev(gc_r), dev(A_r), dev(h_r), scale, chunk_size=C)
+    assert_close("o", o, O.chunk_gla_fwd_o_gk(q, v, gc_r, A_r, h_r, scale, None, C), **FP32)
+    dh_r, dh0_r = O.chunk_bwd_dh(q, k, v, gc_r, do, h0, None, scale, None, C)
+    from tops.ops.common.chunk_h import chunk_bwd_dh_ref
+    dh, dh0 = chunk_bwd_dh_ref(dev(q), dev(k), dev(v), dev(gc_r), dev(do), h0=dev(h0), scale=scale, chunk_size=C)
+    assert_close("dh", dh, dh_r, **FP32)
+    assert_close("dh0", dh0, dh0_r, **FP32)
+    dA_r = O.chunk_gla_bwd_dA(v, do, scale, None, C)
+    assert_close("dA", gla.chunk_gla_bwd_dA_ref(dev(v), dev(do), scale, chunk_size=C), dA_r, **FP32)
+    dv_r = O.chunk_gla_bwd_dv(k, gc_r, A_r, do, dh_r, None, C)
+    assert_close("dv", gla.chunk_gla_bwd_dv_ref(dev(k), dev(gc_r), dev(A_r), dev(do), dev(dh_r), chunk_size=C),
+                 dv_r, **FP32)
+    dqi_r, dki_r = O.chunk_gla_bwd_dqk_intra(q, k, gc_r, dA_r, None, C)
+    dqi, dki = gla.chunk_gla_bwd_dqk_intra_ref(dev(q), dev(k), dev(gc_r), dev(dA_r), chunk_size=C)
+    assert_close("dq_intra", dqi, dqi_r, **FP32)
+    assert_close("dk_intra", dki, dki_r, **FP32)
+    r = O.chunk_gla_bwd_dqkg(q, k, v, h_r, gc_r, do, dh_r, dqi_r, dki_r, scale, None, C)
+    got = gla.chunk_gla_bwd_dqkg_ref(dev(q), dev(k), dev(v), dev(h_r), dev(gc_r), dev(do), dev(dh_r), dev(dqi_r),
+                                     dev(dki_r), scale, chunk_size=C)
+    for nm, a, b in zip(("dq", "dk", "dg"), got, r):
+        assert_close(nm, a, b, **FP32)
+
+
+# ---------------------------------------------------------------------------
+# structural behaviour (reference test_pallas_chunk_gla.py:223-273)
+# ---------------------------------------------------------------------------
+
+def test_state_split(gla):
+    rng = np.random.default_rng(77)
+    B, T, H, K, V = 1, 40, 2, 16, 32
+    q, k = (dev(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = dev(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = dev(GC.logsigmoid(rng.standard_normal((B, T, H, K))).astype(np.float32))
+    o, s = gla.chunk_gla(q, k, v, g, output_final_state=True)
+    o1, s1 = gla.chunk_gla(q[:, :20], k[:, :20], v[:, :20], g[:, :20], output_final_state=True)
+    o2, s2 = gla.chunk_gla(q[:, 20:], k[:, 20:], v[:, 20:], g[:, 20:], initial_state=s1, output_final_state=True)
+    assert_close("o split", torch.cat([o1, o2], 1), o, atol=1e-4, rtol=1e-4)
+    assert_close("state split", s2, s, atol=1e-4, rtol=1e-4)
+
+
+def test_no_final_state_returns_none(gla):
+    x = torch.randn(2, 32, 4, 32, device="cuda")
+    o, s = gla.chunk_gla(x, x, torch.randn(2, 32, 4, 64, device="cuda"), torch.zeros_like(x))
+    assert s is None and o.shape == (2, 32, 4, 64)
+    o, s = gla.fused_recurrent_gla(x, x, torch.randn(2, 32, 4, 64, device="cuda"))
+    assert s is None and o.dtype == torch.float32
+
+
+def test_fused_chunk_and_naive_agree(gla):
+    rng = np.random.default_rng(9)
+    B, T, H, K, V = 2, 70, 2, 32, 32
+    q, k = (dev(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = dev(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = dev(GC.logsigmoid(rng.standard_normal((B, T, H, K))).astype(np.float32))
+    o1, s1 = gla.fused_chunk_gla(q, k, v, g, output_final_state=True)
+    o2, s2 = gla.naive_recurrent_gla(q, k, v, g, output_final_state=True)
+    o3, s3 = gla.chunk_gla(q, k, v, g, output_final_state=True, chunk_size=64)
+    assert_close("fused_chunk vs naive", o1, o2, atol=1e-4, rtol=1e-4)
+    assert_close("chunk64 vs naive", o3, o2, atol=1e-4, rtol=1e-4)
+    assert_close("states", s1, s2, atol=1e-4, rtol=1e-4)
+
+
+def test_g_gamma_matches_broadcast_g(gla):
+    rng = np.random.default_rng(12)
+    B, T, H, K, V = 2, 48, 4, 32, 32
+    q, k = (dev(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = dev(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    gamma = dev(-np.abs(rng.standard_normal((H, 1)).astype(np.float32)) * 0.1)
+    o1, _ = gla.chunk_gla(q, k, v, g_gamma=gamma)
+    o2, _ = gla.chunk_gla(q, k, v, g=gamma.expand(B, T, H, K).contiguous())
+    assert_close("g_gamma", o1, o2, atol=1e-5, rtol=1e-5)
+
+
+def test_errors_are_raised_not_faulted(gla):
+    x = torch.randn(2, 32, 4, 32, device="cuda")
+    with pytest.raises(AssertionError):
+        gla.chunk_gla(x, x[:, :16], x, x)
+    with pytest.raises(AssertionError):
+        gla.chunk_gla(x, x, x, x, chunk_size=12)
+    with pytest.raises(ValueError):
+        gla.chunk_gla(x.cpu(), x.cpu(), x.cpu(), x.cpu())
+
+
+# ---------------------------------------------------------------------------
+# fused_recurrent (decode path)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", GC.REC_CASES, ids=lambda c: c["name"])
+def test_recurrent_matches_reference(gla, case):
+    c, inp, fx = GC.load("rec", case["name"])
+    dt = torch.bfloat16 if case.get("bf16") else torch.float32
+    q, k, v = (dev(inp[n], dt) for n in "qkv")
+    o, ht = gla.fused_recurrent_gla(q, k, v, gk=dev(inp["gk"]), gv=dev(inp["gv"]), scale=inp["scale"],
+                                    initial_state=dev(inp["h0"]), output_final_state=True, reverse=inp["reverse"],
+                                    cu_seqlens=inp["cu"])
+    assert o.dtype == torch.float32 and ht.dtype == torch.float32
+    assert_close("o", o, fx["o"], **FP32)
+    assert_close("ht", ht, fx["ht"], **FP32)
+    dq, dk, dv, dgk, dgv, dh0 = gla.fused_recurrent_gla_bwd(
+        q, k, v, gk=dev(inp["gk"]), gv=dev(inp["gv"]), o=o, do=dev(inp["do"], dt), dht=dev(inp["dht"]),
+        scale=inp["scale"], initial_state=dev(inp["h0"]), reverse=inp["reverse"], cu_seqlens=inp["cu"])
+    for nm, got in (("dq", dq), ("dk", dk), ("dv", dv), ("dgk", dgk), ("dgv", dgv), ("dh0", dh0)):
+        if nm in fx:
+            assert_close(nm, got, fx[nm], atol=2e-4, rtol=2e-4)
+        else:
+            assert got is None, nm
+    if "naive_o" in fx:
+        on, hn = gla.naive_recurrent_gla(q, k, v, dev(inp["gk"]), scale=inp["scale"], initial_state=dev(inp["h0"]),
+                                         output_final_state=True, cu_seqlens=inp["cu"])
+        assert_close("naive_o", on.float(), fx["naive_o"], **FP32)
+
+
+def test_decode_config2_shape_vs_oracle(gla):
+    """BASELINE config 2 at full size: B256 T1 H16 K128 V128, bf16 q/k/v, fp32 gk/h0."""
+    torch.manual_seed(0)
+    B, H, K, V = 256, 16, 128, 128
+    q, k, v = (torch.randn(B, 1, H, D, device="cuda").bfloat16() for D in (K, K, V))
+    gk = torch.nn.functional.logsigmoid(torch.randn(B, 1, H, K, device="cuda")) / 16
+    h0 = torch.randn(B, H, K, V, device="cuda") * 0.1
+    o, ht = gla.fused_recurrent_gla(q, k, v, gk=gk, initial_state=h0, output_final_state=True)
+    # exact fp64 recurrence for one step: h = h0 * e^gk + k v^T ; o = scale q^T h
+    qd, kd, vd = (x.double() for x in (q, k, v))
+    hd = h0.double() * gk.double().exp()[:, 0, :, :, None] + kd[:, 0, :, :, None] * vd[:, 0, :, None, :]
+    od = torch.einsum("bhk,bhkv->bhv", qd[:, 0] * K ** -0.5, hd)[:, None]
+    assert_close("ht", ht, hd, atol=1e-5, rtol=1e-5)
+    assert_close("o", o, od, atol=1e-4, rtol=1e-4)
+
+
+def test_recurrent_autograd(gla):
+    rng = np.random.default_rng(21)
+    B, T, H, K, V = 2, 9, 2, 16, 24
+    q, k = (dev(rng.standard_normal((B, T, H, K), dtype=np.float32)).requires_grad_() for _ in range(2))
+    v = dev(rng.standard_normal((B, T, H, V), dtype=np.float32)).requires_grad_()
+    gk = dev(GC.logsigmoid(rng.standard_normal((B, T, H, K))).astype(np.float32)).requires_grad_()
+    h0 = dev(rng.standard_normal((B, H, K, V), dtype=np.float32)).requires_grad_()
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    dht = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    o, ht = gla.fused_recurrent_gla(q, k, v, gk=gk, initial_state=h0, output_final_state=True)
+    ((o * dev(do)).sum() + (ht * dev(dht)).sum()).backward()
+    ref = O.fused_recurrent_gla_bwd(*(x.detach().cpu().numpy() for x in (q, k, v, gk)), None, do, dht, None,
+                                    h0.detach().cpu().numpy())
+    for nm, t, r in (("dq", q, ref[0]), ("dk", k, ref[1]), ("dv", v, ref[2]), ("dgk", gk, ref[3]),
+                     ("dh0", h0, ref[5])):
+        assert_close(nm, t.grad, r, atol=2e-4, rtol=2e-4)
+
+
+def test_recurrent_k_split(gla):
+    """K > 256 takes the K-split path with a workspace reduction."""
+    rng = np.random.default_rng(5)
+    B, T, H, K, V = 1, 5, 2, 320, 64
+    q, k = (rng.standard_normal((B, T, H, K), dtype=np.float32) for _ in range(2))
+    v = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    gk = GC.logsigmoid(rng.standard_normal((B, T, H, K))).astype(np.float32)
+    o_r, ht_r = O.fused_recurrent_gla(q, k, v, gk, output_final_state=True)
+    o, ht = gla.fused_recurrent_gla(dev(q), dev(k), dev(v), gk=dev(gk), output_final_state=True)
+    assert_close("o", o, o_r, **FP32)
+    assert_close("ht", ht, ht_r, **FP32)
