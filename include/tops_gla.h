@@ -90,6 +90,9 @@ TOPS_API uint64_t tops_gla_launch_count(void);
 TOPS_API void tops_gla_timing_enable(int32_t on);
 TOPS_API int32_t tops_gla_timing_collect(char* names, int32_t name_stride, float* ms, int32_t max_entries);
 TOPS_API int32_t tops_gla_abi_version(void);
+/* First error code recorded by a device-side bounded wait since the last call
+ * (0 = none, 1 = an mbarrier wait timed out); reading clears it.  Synchronizes. */
+TOPS_API int32_t tops_gla_device_error(void);
 /* 1 when the current device can run the tcgen05 (sm_100a) kernels. */
 TOPS_API int32_t tops_gla_has_tcgen05(void);
 

@@ -112,6 +112,10 @@ size_t bwd_workspace(const tops_gla_recurrent_bwd_args& a);
 int bwd(const tops_gla_recurrent_bwd_args& a, cudaStream_t st);
 }  // namespace rec
 
+namespace decode {
+int read_device_error();
+}  // namespace decode
+
 namespace seqpar {
 int span_decay(const tops_gla_shape& s, const float* g, float* decay, cudaStream_t st);
 int state_combine(int N, int H, int K, int V, const float* decay, const float* h_in, const float* s_local,
@@ -242,6 +246,11 @@ extern "C" {
 
 const char* tops_gla_last_error(void) { return g_last_error.c_str(); }
 uint64_t tops_gla_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int32_t tops_gla_device_error(void) {
+  int32_t e = decode::read_device_error();
+  return e;
+}
 
 void tops_gla_timing_enable(int32_t on) {
   std::lock_guard<std::mutex> lk(g_timing_mu);

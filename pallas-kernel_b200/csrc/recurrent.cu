@@ -195,6 +195,13 @@ static void plan(int K, int& rows, int& splits) {
 
 static bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+}  // namespace rec
+namespace decode {
+bool supported(const tops_gla_recurrent_args& a);
+int fwd(const tops_gla_recurrent_args& a, cudaStream_t st);
+}  // namespace decode
+namespace rec {
+
 size_t fwd_workspace(const tops_gla_recurrent_args& a) {
   int rows, splits;
   plan(a.K, rows, splits);
@@ -204,6 +211,7 @@ size_t fwd_workspace(const tops_gla_recurrent_args& a) {
 
 int fwd(const tops_gla_recurrent_args& a, cudaStream_t st) {
   if ((size_t)a.B * a.T * a.H == 0 && a.ht == nullptr) return TOPS_OK;
+  if (decode::supported(a)) return decode::fwd(a, st);
   int rows, splits;
   plan(a.K, rows, splits);
   const size_t need = fwd_workspace(a);

@@ -277,7 +277,8 @@ def test_recurrent_matches_reference(gla, case):
     if "naive_o" in fx:
         on, hn = gla.naive_recurrent_gla(q, k, v, dev(inp["gk"]), scale=inp["scale"], initial_state=dev(inp["h0"]),
                                          output_final_state=True, cu_seqlens=inp["cu"])
-        assert_close("naive_o", on.float(), fx["naive_o"], **FP32)
+        tol = FP32 if dt == torch.float32 else dict(atol=1e-2, rtol=1e-2)  # naive returns o in q's dtype
+        assert_close("naive_o", on.float(), fx["naive_o"], **tol)
 
 
 def test_decode_config2_shape_vs_oracle(gla):
@@ -325,3 +326,29 @@ def test_recurrent_k_split(gla):
     o, ht = gla.fused_recurrent_gla(dev(q), dev(k), dev(v), gk=dev(gk), output_final_state=True)
     assert_close("o", o, o_r, **FP32)
     assert_close("ht", ht, ht_r, **FP32)
+
+
+def test_no_device_side_timeouts(gla):
+    """No bounded device wait gave up during the tests above (error word stays 0)."""
+    from tops import _C
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
+
+
+def test_decode_general_shapes(gla):
+    """Streaming decode kernel (T == 1): gates on/off, no h0, no ht, several V."""
+    rng = np.random.default_rng(31)
+    for (B, H, K, V, gk_on, gv_on, h0_on) in [(3, 5, 64, 64, True, True, True), (2, 3, 128, 32, False, False, False),
+                                              (4, 2, 32, 256, True, False, True), (1, 7, 128, 128, False, True, True)]:
+        q, k = (rng.standard_normal((B, 1, H, K), dtype=np.float32) for _ in range(2))
+        v = rng.standard_normal((B, 1, H, V), dtype=np.float32)
+        gk = GC.logsigmoid(rng.standard_normal((B, 1, H, K))).astype(np.float32) if gk_on else None
+        gv = GC.logsigmoid(rng.standard_normal((B, 1, H, V))).astype(np.float32) if gv_on else None
+        h0 = rng.standard_normal((B, H, K, V), dtype=np.float32) if h0_on else None
+        o_r, ht_r = O.fused_recurrent_gla(q, k, v, gk, gv, None, h0, True)
+        for want_ht in (True, False):
+            o, ht = gla.fused_recurrent_gla(dev(q), dev(k), dev(v), gk=dev(gk), gv=dev(gv), initial_state=dev(h0),
+                                            output_final_state=want_ht)
+            assert_close("o", o, o_r, **FP32)
+            if want_ht:
+                assert_close("ht", ht, ht_r, **FP32)
