@@ -140,6 +140,21 @@ typedef struct tops_gla_chunk_bwd_args {
  * Replaces tops.ops.gla.chunk_gla_bwd (tops/ops/gla/chunk.py:815) and
  * chunk_gla_bwd_with_pl (tops/ops/gla/chunk.py:980). */
 TOPS_API int tops_gla_chunk_bwd(const tops_gla_chunk_bwd_args* a, void* stream);
+
+/* Chunked GLA forward that allocates nothing and needs no workspace.  No counterpart
+ * in the reference (whose JAX ops get their memory from XLA): it exists for callers
+ * that cannot call cudaMalloc or pass a scratch buffer -- e.g. a host framework that
+ * plans all device memory up front and gives an operator only its inputs and
+ * outputs, or a serving loop that must not call the allocator.  Same arguments and
+ * results as tops_gla_chunk_fwd; a->workspace is ignored.  Scratch comes from a
+ * fixed array of TOPS_GLA_NOALLOC_SCRATCH_BYTES inside the library's device image,
+ * one per GPU that loads the library, held until the process exits.  Problems whose
+ * scratch (tops_gla_chunk_fwd_workspace_size) exceeds it are rejected with
+ * TOPS_ERR_WORKSPACE.  The first call on a device looks up that device's array
+ * address (make it before any stream capture).  All calls on a device share the
+ * array: calls whose kernels overlap on the GPU race. */
+#define TOPS_GLA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+TOPS_API int tops_gla_chunk_fwd_noalloc(const tops_gla_chunk_fwd_args* a, void* stream);
 TOPS_API size_t tops_gla_chunk_bwd_workspace_size(const tops_gla_chunk_bwd_args* a);
 
 typedef struct tops_gla_recurrent_args {

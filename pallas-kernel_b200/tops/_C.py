@@ -73,6 +73,7 @@ SIGNATURES = {
     "tops_gla_chunk_fwd": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
     "tops_gla_chunk_fwd_workspace_size": (C.c_size_t, [C.POINTER(ChunkFwdArgs)]),
     "tops_gla_chunk_bwd": (C.c_int, [C.POINTER(ChunkBwdArgs), VP]),
+    "tops_gla_chunk_fwd_noalloc": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
     "tops_gla_chunk_bwd_workspace_size": (C.c_size_t, [C.POINTER(ChunkBwdArgs)]),
     "tops_gla_recurrent_fwd": (C.c_int, [C.POINTER(RecArgs), VP]),
     "tops_gla_recurrent_fwd_workspace_size": (C.c_size_t, [C.POINTER(RecArgs)]),
