@@ -267,9 +267,9 @@ def run_ours(args):
     plan = _core.make_plan(q, V, C, None, K ** -0.5)
 
     def step():
-        o, _, saved = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
-        gc, A, h = saved
-        return _core.chunk_bwd(plan, q, k, v, g, None, do, None, gc, A, h, False)
+        o, _, sv = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+        return _core.chunk_bwd(plan, q, k, v, g, None, do, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"), False,
+                               block=sv.get("block"))
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 3)):
@@ -404,9 +404,9 @@ def e2e_bench(args, world, dev, q, k, v, g, do, plan):
     def step():
         dq_, dk_, dv_, dg_ = (x.to(dev, non_blocking=True) for x in (hq, hk, hv, hg))
         ddo = hdo.to(dev, non_blocking=True)
-        o, _, saved = _core.chunk_fwd(plan, dq_, dk_, dv_, dg_, None, False, save=True)
-        gc, A, h = saved
-        r = _core.chunk_bwd(plan, dq_, dk_, dv_, dg_, None, ddo, None, gc, A, h, False)
+        o, _, sv = _core.chunk_fwd(plan, dq_, dk_, dv_, dg_, None, False, save=True)
+        r = _core.chunk_bwd(plan, dq_, dk_, dv_, dg_, None, ddo, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
+                            False, block=sv.get("block"))
         for dst, src in zip(outs, r[:4]):
             dst.copy_(src, non_blocking=True)
 

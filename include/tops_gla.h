@@ -112,6 +112,10 @@ typedef struct tops_gla_chunk_fwd_args {
   float* A;                    /* [B,T,H,C] */
   float* h;                    /* [NT,H,K,V] */
   void* workspace; size_t workspace_bytes;
+  /* Opaque block receiving what the backward reuses when the forward runs on the
+   * tensor-core path (bf16, K in {128, 256}, V % 128 == 0, fixed length); size from
+   * tops_gla_chunk_saved_size(), NULL = do not save.  Pass it to the backward. */
+  void* saved; size_t saved_bytes;
 } tops_gla_chunk_fwd_args;
 
 /* Chunked GLA forward: o = chunk_gla(q,k,v,g,scale,h0)[0], ht = final state.
@@ -119,6 +123,9 @@ typedef struct tops_gla_chunk_fwd_args {
  * and fused_chunk_gla (tops/ops/gla/fused_chunk.py:4). */
 TOPS_API int tops_gla_chunk_fwd(const tops_gla_chunk_fwd_args* a, void* stream);
 TOPS_API size_t tops_gla_chunk_fwd_workspace_size(const tops_gla_chunk_fwd_args* a);
+/* Bytes of the forward's saved block for this problem; 0 when the problem runs on
+ * the CUDA-core path (which saves into the g_cumsum / A / h arguments instead). */
+TOPS_API size_t tops_gla_chunk_saved_size(const tops_gla_shape* s);
 
 typedef struct tops_gla_chunk_bwd_args {
   tops_gla_shape s;
@@ -134,6 +141,7 @@ typedef struct tops_gla_chunk_bwd_args {
   float* dg;                   /* out [B,T,H,K] fp32 */
   float* dh0;                  /* out [N,H,K,V] or NULL */
   void* workspace; size_t workspace_bytes;
+  const void* saved; size_t saved_bytes;  /* block written by the forward, or NULL */
 } tops_gla_chunk_bwd_args;
 
 /* Chunked GLA backward -> dq, dk, dv, dg, dh0.

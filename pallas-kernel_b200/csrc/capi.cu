@@ -116,6 +116,14 @@ namespace decode {
 int read_device_error();
 }  // namespace decode
 
+namespace tc {
+bool eligible(const tops_gla_shape& s);
+size_t saved_bytes(const tops_gla_shape& s);
+int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        void* o, float* ht, void* saved, cudaStream_t st);
+int read_device_error();
+}  // namespace tc
+
 namespace seqpar {
 int span_decay(const tops_gla_shape& s, const float* g, float* decay, cudaStream_t st);
 int state_combine(int N, int H, int K, int V, const float* decay, const float* h_in, const float* s_local,
@@ -135,12 +143,32 @@ static int check_simt_chunk(const tops_gla_shape& s) {
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
+// the tensor-core path serves bf16 problems that ask for no CUDA-core-format intermediates
+static bool use_tc_fwd(const tops_gla_chunk_fwd_args* a) {
+  return a->g != nullptr && a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
+}
+
 static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t* ws_need) {
   int rc = check_shape(a ? &a->s : nullptr);
   if (rc) return rc;
   const tops_gla_shape& s = a->s;
-  if ((rc = check_simt_chunk(s))) return rc;
   const bool dry = ws_need != nullptr;
+  if (use_tc_fwd(a)) {
+    const size_t need_saved = tc::saved_bytes(s);
+    const bool own = a->saved != nullptr;
+    if (own && a->saved_bytes < need_saved)
+      return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: saved block smaller than tops_gla_chunk_saved_size()");
+    if (dry) {
+      *ws_need = own ? 0 : need_saved;
+      return TOPS_OK;
+    }
+    TOPS_CHECK_ARG(a->q && a->k && a->v && a->o, "chunk_fwd: q, k, v and o are required");
+    void* blk = own ? a->saved : a->workspace;
+    if (!own && (a->workspace == nullptr || a->workspace_bytes < need_saved))
+      return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: workspace smaller than tops_gla_chunk_fwd_workspace_size()");
+    return tc::fwd(s, a->q, a->k, a->v, a->g, a->h0, a->o, a->ht, blk, S(stream));
+  }
+  if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {
     TOPS_CHECK_ARG(a->q && a->k && a->v && a->o, "chunk_fwd: q, k, v and o are required");
   }
@@ -249,7 +277,13 @@ uint64_t tops_gla_launch_count(void) { return g_launches.load(std::memory_order_
 
 int32_t tops_gla_device_error(void) {
   int32_t e = decode::read_device_error();
-  return e;
+  const int32_t e2 = tc::read_device_error();
+  return e != 0 ? e : e2;
+}
+
+size_t tops_gla_chunk_saved_size(const tops_gla_shape* s) {
+  if (check_shape(s) != TOPS_OK || !tc::eligible(*s)) return 0;
+  return tc::saved_bytes(*s);
 }
 
 void tops_gla_timing_enable(int32_t on) {

@@ -1,0 +1,653 @@
+// tcgen05 (5th-gen tensor core) kernels of the bf16 chunked GLA path on sm_100a.
+//
+// Math (reference tops/ops/gla/chunk.py:1083-1179 forward, 815-977 backward;
+// tops/ops/common/chunk_h.py:277-492 state scans), with chunks of BT = 128 tokens
+// (the result is independent of the chunk length in exact arithmetic; 128 matches
+// the M = 128 tcgen05 tile):
+//   G      = chunk-local cumsum of g;  GL = G at the chunk's last row;  Gm = G at row 63
+//   qhat   = scale q e^{G}           kdec = k e^{GL - G}           D = e^{GL}
+//   A      = scale tril((q e^{G-Gm}) (k e^{Gm-G})^T)     (mid-chunk reference row)
+//   h_{c+1}= D_c * h_c + kdec_c^T v_c          (state scan, fp32 state in TMEM)
+//   o_c    = qhat_c h_c + A_c v_c              (one GEMM over [qhat | A] x [h ; v])
+// Backward pieces reuse the same kernels: the reverse scan dh_{c-1} = D_c dh_c +
+// qhat_c^T do_c and dv_c = A_c^T do_c + kdec_c dh_c.
+//
+// Kernels
+//   k_prep : per (batch, chunk, head).  TMA loads q/k/g tiles, computes the gates in
+//            registers, writes qhat/kdec (TMA store) and D, and the intra-chunk matrix
+//            A with tcgen05.mma (accumulator in TMEM).
+//   k_scan : per (batch, head, 128-wide V tile).  Walks the chunks in order (or in
+//            reverse), state [K x 128] fp32 resident in TMEM, operands double
+//            buffered by TMA; optionally stores every chunk-start state in bf16.
+//   k_out  : persistent, warp specialised GEMM: TMA producer warp, MMA warp, four
+//            epilogue warps; 6-stage shared-memory ring, double-buffered TMEM
+//            accumulator.  out[128 x 128] = X[128 x K] S[K x 128] + A'[128 x 128] Y[128 x 128].
+// All waits are bounded (ptx::mbar_wait).  Shared-memory tiles use the 128-byte
+// swizzle that TMA writes and the UMMA descriptors describe.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace tops {
+namespace tc {
+
+constexpr int BT = 128;   // chunk length (tokens)
+constexpr int BV = 128;   // V tile
+constexpr int TILE_BYTES = 128 * 128;  // one [128 rows][64 bf16] swizzled tile = 16 KB
+
+using bf16 = __nv_bfloat16;
+
+// ---------------------------------------------------------------------------
+// host: tensor maps
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// rank-4 map over a [B, T, H, D] tensor: dims {D, H, T, B}; box {bx, 1, by, 1}
+static bool map_tok(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int es, int B, int T, int H, int D,
+                    int bx, int by) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)D * es, (cuuint64_t)H * D * es, (cuuint64_t)T * H * D * es};
+  cuuint32_t box[4] = {(cuuint32_t)bx, 1, (cuuint32_t)by, 1};
+  cuuint32_t es1[4] = {1, 1, 1, 1};
+  return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, es1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// rank-3 map over per-chunk states [R, K, V] (R = chunks*heads): dims {V, K, R}; box {64, by, 1}
+static bool map_state(CUtensorMap* m, const void* base, int R, int K, int V, int by) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)V, (cuuint64_t)K, (cuuint64_t)R};
+  cuuint64_t strides[2] = {(cuuint64_t)V * 2, (cuuint64_t)K * V * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)by, 1};
+  cuuint32_t es1[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es1,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t desc_kmajor(const void* tile, uint32_t byte_off) {
+  return ptx::sdesc_sw128(ptx::smem_u32(tile) + byte_off, 16, 1024);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor(const void* tile, uint32_t byte_off, uint32_t mn_block_stride) {
+  return ptx::sdesc_sw128(ptx::smem_u32(tile) + byte_off, mn_block_stride, 1024);
+}
+__device__ __forceinline__ float bf(const unsigned char* tile, uint32_t row, uint32_t col) {
+  return __bfloat162float(*reinterpret_cast<const bf16*>(tile + ptx::sw128(row, col * 2)));
+}
+__device__ __forceinline__ void st_bf(unsigned char* tile, uint32_t row, uint32_t col, float x) {
+  *reinterpret_cast<bf16*>(tile + ptx::sw128(row, col * 2)) = __float2bfloat16_rn(x);
+}
+__device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, uint32_t lane0, uint32_t col) {
+  return base + (lane0 << 16) + col;
+}
+
+// ===========================================================================
+// k_prep: gates, qhat/kdec, D and the intra-chunk matrix A.  grid (NTb, H, B), 256 threads.
+// ===========================================================================
+struct PrepParams {
+  int B, T, H, K, NTb;
+  float scale;
+  float* D;  // [B*NTb, H, K]
+};
+
+struct PrepMaps {
+  CUtensorMap q, k, g, qh, kd, A;
+};
+
+__global__ void __launch_bounds__(256, 1) k_prep(const __grid_constant__ PrepMaps maps, PrepParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* qb = smem;                   // [128][64] bf16: q -> qhat (in place)
+  unsigned char* kb = qb + TILE_BYTES;        // k -> kdec
+  unsigned char* gb = kb + TILE_BYTES;        // 2 x [128][32] fp32
+  unsigned char* qt = gb + 2 * TILE_BYTES;    // q e^{G-Gm}
+  unsigned char* kt = qt + TILE_BYTES;        // k e^{Gm-G}
+  __shared__ float psum[4][64];
+  __shared__ __align__(8) uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = c * BT;
+  const int nkb = p.K / 64;
+
+  if (warp == 0) {
+    ptx::tmem_alloc(&tmem_base, 128);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 0) {
+    ptx::mbar_init(&bar_load, 1);
+    ptx::mbar_init(&bar_mma, 1);
+    ptx::fence_mbar_init();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tacc = tmem_base;
+  constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, false, false);
+
+  // gating thread mapping: part (32 rows) x column (64 per K block)
+  const int part = warp >> 1, col = (warp & 1) * 32 + lane;
+  bool ok = true;
+  for (int kbi = 0; kbi < nkb && ok; ++kbi) {
+    if (tid == 0) {
+      if (kbi > 0) ptx::bulk_wait_read<0>();  // previous qhat/kdec stores have read qb/kb
+      ptx::mbar_arrive_expect_tx(&bar_load, 4 * TILE_BYTES);
+      ptx::tma_load_4d(qb, &maps.q, kbi * 64, h, row0, b, &bar_load);
+      ptx::tma_load_4d(kb, &maps.k, kbi * 64, h, row0, b, &bar_load);
+      ptx::tma_load_4d(gb, &maps.g, kbi * 64, h, row0, b, &bar_load);
+      ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, kbi * 64 + 32, h, row0, b, &bar_load);
+    }
+    ok = ptx::mbar_wait(&bar_load, (uint32_t)(kbi & 1));
+    if (!ok) break;
+    // g(row, col): fp32 tile (col / 32), byte (col % 32) * 4
+    const unsigned char* gt = gb + (col >> 5) * TILE_BYTES;
+    const uint32_t gbyte = (uint32_t)(col & 31) * 4;
+    float s = 0.f;
+    for (int r = part * 32; r < part * 32 + 32; ++r) s += *reinterpret_cast<const float*>(gt + ptx::sw128(r, gbyte));
+    psum[part][col] = s;
+    __syncthreads();
+    float off = 0.f;
+    for (int pp = 0; pp < part; ++pp) off += psum[pp][col];
+    const float GL = psum[0][col] + psum[1][col] + psum[2][col] + psum[3][col];
+    const float Gm = psum[0][col] + psum[1][col];
+    const float eGm = __expf(Gm), eGLm = __expf(GL - Gm);
+    if (part == 0) p.D[((size_t)(b * p.NTb + c) * p.H + h) * p.K + kbi * 64 + col] = __expf(GL);
+    float run = off;
+    for (int r = part * 32; r < part * 32 + 32; ++r) {
+      run += *reinterpret_cast<const float*>(gt + ptx::sw128(r, gbyte));
+      const float a = __expf(run - Gm), bb = __expf(Gm - run);
+      const float qv = bf(qb, r, col), kv = bf(kb, r, col);
+      st_bf(qt, r, col, qv * a);
+      st_bf(kt, r, col, kv * bb);
+      st_bf(qb, r, col, p.scale * qv * a * eGm);
+      st_bf(kb, r, col, kv * bb * eGLm);
+    }
+    ptx::fence_async_smem();
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        ptx::mma_bf16_ss(tacc, desc_kmajor(qt, ks * 32), desc_kmajor(kt, ks * 32), IDESC, (kbi | ks) ? 1u : 0u);
+      ptx::mma_commit(&bar_mma);
+      ptx::tma_store_4d(&maps.qh, kbi * 64, h, row0, b, qb);
+      ptx::tma_store_4d(&maps.kd, kbi * 64, h, row0, b, kb);
+      ptx::bulk_commit();
+    }
+    ok = ptx::mbar_wait(&bar_mma, (uint32_t)(kbi & 1));
+    ptx::tc_fence_after();
+  }
+  if (ok) {
+    // epilogue: A (TMEM, 128 x 128 fp32) -> causal mask, scale -> bf16 -> qt | kt -> TMA store
+    const int qd = warp & 3, ch = warp >> 2;  // lane quadrant, column half
+    const int i = qd * 32 + lane;
+    unsigned char* stg = ch ? kt : qt;
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+      float r[32];
+      ptx::tmem_ld32(tmem_lane_addr(tacc, qd * 32, ch * 64 + cb * 32), r);
+      ptx::tmem_ld_wait();
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j0 = ch * 64 + cb * 32 + j4 * 8 + 2 * u;
+          const float a0 = (j0 <= i) ? r[j4 * 8 + 2 * u] * p.scale : 0.f;
+          const float a1 = (j0 + 1 <= i) ? r[j4 * 8 + 2 * u + 1] * p.scale : 0.f;
+          w[u] = ptx::pack_bf16(a0, a1);
+        }
+        *reinterpret_cast<uint4*>(stg + ptx::sw128(i, (cb * 32 + j4 * 8) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    ptx::fence_async_smem();
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      ptx::tma_store_4d(&maps.A, 0, h, row0, b, qt);
+      ptx::tma_store_4d(&maps.A, 64, h, row0, b, kt);
+      ptx::bulk_commit();
+    }
+  }
+  if (tid == 0) ptx::bulk_wait<0>();
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tacc, 128);
+}
+
+// ===========================================================================
+// k_scan: state scan over chunks.  grid (V/128, H, B), 256 threads.
+// ===========================================================================
+struct ScanParams {
+  int B, T, H, K, V, NTb, reverse;
+  const float* D;     // [B*NTb, H, K]
+  const float* init;  // [B, H, K, V] fp32 or null
+  float* fin;         // [B, H, K, V] fp32 or null
+  bf16* states;       // [B*NTb, H, K, V] bf16 (chunk-start states) or null
+};
+
+struct ScanMaps {
+  CUtensorMap x, y;  // x: [B,T,H,K] bf16 box (64,1,128,1); y: [B,T,H,V] bf16 box (64,1,128,1)
+};
+
+__global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMaps maps, ScanParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nkb = p.K / 64;              // X tiles per chunk
+  const int nh = p.K / 128;              // state halves (TMEM lane blocks)
+  const uint32_t buf_bytes = (uint32_t)(nkb + 2) * TILE_BYTES;
+  __shared__ __align__(8) uint64_t bar_full[2], bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int vt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int v0 = vt * BV;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2;  // lane quadrant, state half handled by this warp
+  const int krow = hf * 128 + qd * 32 + lane;
+  const bool active = hf < nh;
+
+  if (warp == 0) {
+    ptx::tmem_alloc(&tmem_base, 256);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 0) {
+    ptx::mbar_init(&bar_full[0], 1);
+    ptx::mbar_init(&bar_full[1], 1);
+    ptx::mbar_init(&bar_mma, 1);
+    ptx::fence_mbar_init();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tstate = tmem_base;
+  constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, true, true);
+
+  auto chunk_of = [&](int i) { return p.reverse ? p.NTb - 1 - i : i; };
+  auto issue = [&](int i) {
+    const int c = chunk_of(i);
+    unsigned char* buf = smem + (i & 1) * buf_bytes;
+    ptx::mbar_arrive_expect_tx(&bar_full[i & 1], buf_bytes);
+    for (int j = 0; j < nkb; ++j) ptx::tma_load_4d(buf + j * TILE_BYTES, &maps.x, j * 64, h, c * BT, b, &bar_full[i & 1]);
+    ptx::tma_load_4d(buf + nkb * TILE_BYTES, &maps.y, v0, h, c * BT, b, &bar_full[i & 1]);
+    ptx::tma_load_4d(buf + (nkb + 1) * TILE_BYTES, &maps.y, v0 + 64, h, c * BT, b, &bar_full[i & 1]);
+  };
+  if (tid == 0) {
+    issue(0);
+    if (p.NTb > 1) issue(1);
+  }
+  // initial state -> TMEM
+  if (active) {
+    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0;
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      float r[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[srow + cb * 32 + j] : 0.f;
+      ptx::tmem_st32(tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32), r);
+    }
+    ptx::tmem_st_wait();
+  }
+  bool ok = true;
+  for (int i = 0; i < p.NTb; ++i) {
+    const int c = chunk_of(i);
+    if (i > 0) {
+      ok = ptx::mbar_wait(&bar_mma, (uint32_t)((i - 1) & 1));
+      ptx::tc_fence_after();
+      if (!ok) break;
+      if (tid == 0 && i + 1 < p.NTb) issue(i + 1);  // buffer (i+1)&1 was read by chunk i-1, now complete
+    }
+    // TMEM pass: store the chunk-start state (bf16), then scale rows by D_c
+    if (active) {
+      const float d = p.D[((size_t)(b * p.NTb + c) * p.H + h) * p.K + krow];
+      const size_t srow = ((size_t)((b * p.NTb + c) * p.H + h) * p.K + krow) * p.V + v0;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float r[32];
+        const uint32_t ta = tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32);
+        ptx::tmem_ld32(ta, r);
+        ptx::tmem_ld_wait();
+        if (p.states) {
+          uint4* dst = reinterpret_cast<uint4*>(p.states + srow + cb * 32);
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8)
+            dst[j8] = make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
+                                 ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] *= d;
+        ptx::tmem_st32(ta, r);
+      }
+      ptx::tmem_st_wait();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      ok = ptx::mbar_wait(&bar_full[i & 1], (uint32_t)((i >> 1) & 1));
+      if (ok) {
+        ptx::tc_fence_after();
+        const unsigned char* buf = smem + (i & 1) * buf_bytes;
+        const unsigned char* ybuf = buf + nkb * TILE_BYTES;
+        for (int half = 0; half < nh; ++half) {
+          const unsigned char* xa = buf + (2 * half) * TILE_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            ptx::mma_bf16_ss(tstate + half * 128, desc_mnmajor(xa, ks * 2048, TILE_BYTES),
+                             desc_mnmajor(ybuf, ks * 2048, TILE_BYTES), IDESC, 1u);
+        }
+        ptx::mma_commit(&bar_mma);
+      }
+    }
+    // a failed wait in thread 0 leaves bar_mma pending: the next wait times out for everyone
+  }
+  if (ok) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((p.NTb - 1) & 1));
+  ptx::tc_fence_after();
+  if (ok && active && p.fin) {
+    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0;
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      float r[32];
+      ptx::tmem_ld32(tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32), r);
+      ptx::tmem_ld_wait();
+      float4* dst = reinterpret_cast<float4*>(p.fin + srow + cb * 32);
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) dst[j4] = make_float4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+    }
+  }
+  // drain loads that may still be in flight after an early exit
+  if (!ok && tid == 0) {
+    ptx::mbar_wait(&bar_full[0], 0);
+    ptx::mbar_wait(&bar_full[1], 0);
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tstate, 256);
+}
+
+// ===========================================================================
+// k_out: persistent GEMM  out[128 x 128] = X[128 x K] S[K x 128] + A'[128 x 128] Y[128 x 128]
+// per item (batch, chunk, head, V tile).  grid = #SMs, 192 threads.
+//   fwd: X = qhat, S = h_c, A' = A (K-major), Y = v, out = o
+//   bwd: X = kdec, S = dh_c, A' = A^T (M-major), Y = do, out = dv
+// ===========================================================================
+constexpr int OUT_STAGES = 6;
+constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // A tile 16 KB + B tile 16 KB
+
+struct OutParams {
+  int B, T, H, K, V, NTb, trans_a;
+  bf16* out;  // [B, T, H, V]
+};
+
+struct OutMaps {
+  CUtensorMap x;   // [B,T,H,K] box (64,1,128,1)
+  CUtensorMap s;   // [B*NTb*H, K, V] box (64,64,1)
+  CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1); bwd box (64,1,64,1)
+  CUtensorMap y;   // [B,T,H,V] box (64,1,64,1)
+};
+
+__global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps maps, OutParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[OUT_STAGES], empty[OUT_STAGES], accf[2], acce[2];
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nvt = p.V / BV;
+  const int items = p.B * p.NTb * p.H * nvt;
+  const int nkb = p.K / 64 + 2;
+
+  if (warp == 0) {
+    ptx::tmem_alloc(&tmem_base, 256);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int s = 0; s < OUT_STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&accf[a], 1);
+      ptx::mbar_init(&acce[a], 4);
+    }
+    ptx::fence_mbar_init();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tacc = tmem_base;
+
+  auto decode = [&](int it, int& b, int& c, int& h, int& vt) {
+    vt = it % nvt;
+    int r = it / nvt;
+    h = r % p.H;
+    r /= p.H;
+    c = r % p.NTb;
+    b = r / p.NTb;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      uint32_t n = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        int b, c, h, vt;
+        decode(it, b, c, h, vt);
+        const int row0 = c * BT, v0 = vt * BV;
+        const int srow = (b * p.NTb + c) * p.H + h;
+        for (int kb = 0; kb < nkb; ++kb, ++n) {
+          const int s = n % OUT_STAGES;
+          ok = ptx::mbar_wait(&empty[s], ((n / OUT_STAGES) & 1) ^ 1);
+          if (!ok) break;
+          unsigned char* at = smem + s * STAGE_BYTES;
+          unsigned char* bt = at + TILE_BYTES;
+          ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          if (kb < p.K / 64) {
+            ptx::tma_load_4d(at, &maps.x, kb * 64, h, row0, b, &full[s]);
+            ptx::tma_load_3d(bt, &maps.s, v0, kb * 64, srow, &full[s]);
+            ptx::tma_load_3d(bt + TILE_BYTES / 2, &maps.s, v0 + 64, kb * 64, srow, &full[s]);
+          } else {
+            const int j = kb - p.K / 64;  // 64-token block of the intra part
+            if (!p.trans_a) {
+              ptx::tma_load_4d(at, &maps.a, j * 64, h, row0, b, &full[s]);
+            } else {
+              ptx::tma_load_4d(at, &maps.a, 0, h, row0 + j * 64, b, &full[s]);
+              ptx::tma_load_4d(at + TILE_BYTES / 2, &maps.a, 64, h, row0 + j * 64, b, &full[s]);
+            }
+            ptx::tma_load_4d(bt, &maps.y, v0, h, row0 + j * 64, b, &full[s]);
+            ptx::tma_load_4d(bt + TILE_BYTES / 2, &maps.y, v0 + 64, h, row0 + j * 64, b, &full[s]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      uint32_t n = 0, t = 0;
+      bool ok = true;
+      const uint32_t ID_K = ptx::idesc_bf16(128, 128, false, true);
+      const uint32_t ID_M = ptx::idesc_bf16(128, 128, true, true);
+      for (int it = blockIdx.x; it < items && ok; it += gridDim.x, ++t) {
+        const int ab = t & 1;
+        ok = ptx::mbar_wait(&acce[ab], ((t >> 1) & 1) ^ 1);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint32_t d = tacc + ab * 128;
+        for (int kb = 0; kb < nkb; ++kb, ++n) {
+          const int s = n % OUT_STAGES;
+          ok = ptx::mbar_wait(&full[s], (n / OUT_STAGES) & 1);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const unsigned char* at = smem + s * STAGE_BYTES;
+          const unsigned char* bt = at + TILE_BYTES;
+          const bool mn = p.trans_a && kb >= p.K / 64;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t ad = mn ? desc_mnmajor(at, ks * 2048, TILE_BYTES / 2) : desc_kmajor(at, ks * 32);
+            ptx::mma_bf16_ss(d, ad, desc_mnmajor(bt, ks * 2048, TILE_BYTES / 2), mn ? ID_M : ID_K,
+                             (kb | ks) ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[s]);
+        }
+        if (ok) ptx::mma_commit(&accf[ab]);
+      }
+    }
+  } else {  // epilogue warps 2..5: lane quadrant (warp & 3)
+    const int qd = warp & 3;
+    const int i = qd * 32 + lane;
+    uint32_t t = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++t) {
+      int b, c, h, vt;
+      decode(it, b, c, h, vt);
+      const int ab = t & 1;
+      if (!ptx::mbar_wait(&accf[ab], (t >> 1) & 1)) break;
+      ptx::tc_fence_after();
+      const int row = c * BT + i;
+      bf16* dst = p.out + ((size_t)(b * p.T + row) * p.H + h) * p.V + vt * BV;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float r[32];
+        ptx::tmem_ld32(tmem_lane_addr(tacc, qd * 32, ab * 128 + cb * 32), r);
+        ptx::tmem_ld_wait();
+        if (row < p.T) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cb * 32);
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8)
+            d4[j8] = make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
+                                ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&acce[ab]);
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tacc, 256);
+}
+
+TOPS_DEVICE_ERROR_READER(read_device_error)
+
+// ---------------------------------------------------------------------------
+// host orchestration
+// ---------------------------------------------------------------------------
+static int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+bool eligible(const tops_gla_shape& s) {
+  return s.dtype == TOPS_BF16 && s.cu_seqlens == nullptr && (s.K == 128 || s.K == 256) && s.V % BV == 0 &&
+         s.T > 0 && s.B > 0 && s.H > 0 && tops_gla_has_tcgen05() && encode_fn() != nullptr;
+}
+
+// Intermediates of the forward that the backward reuses (one contiguous block).
+struct Saved {
+  bf16 *qh, *kd, *A, *h;
+  float* D;
+};
+
+static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
+  const int NTb = (s.T + BT - 1) / BT;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    off = (off + 1023) & ~size_t(1023);
+    char* p = base ? static_cast<char*>(base) + off : nullptr;
+    off += bytes;
+    return p;
+  };
+  const size_t tok = (size_t)s.B * s.T * s.H;
+  Saved v;
+  v.qh = reinterpret_cast<bf16*>(take(tok * s.K * 2));
+  v.kd = reinterpret_cast<bf16*>(take(tok * s.K * 2));
+  v.A = reinterpret_cast<bf16*>(take(tok * BT * 2));
+  v.D = reinterpret_cast<float*>(take((size_t)s.B * NTb * s.H * s.K * 4));
+  v.h = reinterpret_cast<bf16*>(take((size_t)s.B * NTb * s.H * s.K * s.V * 2));
+  if (sv) *sv = v;
+  return off;
+}
+
+size_t saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nullptr); }
+
+static size_t prep_smem() { return 6 * TILE_BYTES + 1024; }
+static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 1024; }
+static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 1024; }
+
+template <typename KernelT>
+static cudaError_t set_smem(KernelT k, size_t bytes) {
+  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// Forward: o, ht and (in `saved`) qhat, kdec, A, D, chunk-start states h.
+int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        void* o, float* ht, void* saved, cudaStream_t st) {
+  if (g == nullptr) return fail(TOPS_ERR_UNSUPPORTED, "tc fwd needs gates");
+  Saved sv;
+  carve_saved(s, saved, &sv);
+  const int NTb = (s.T + BT - 1) / BT;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  PrepMaps pm;
+  bool okm = map_tok(&pm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&pm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+             map_tok(&pm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
+             map_tok(&pm.qh, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+             map_tok(&pm.kd, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+             map_tok(&pm.A, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
+  ScanMaps sm;
+  okm = okm && map_tok(&sm.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  OutMaps om;
+  okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
+        map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) && map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64);
+  if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
+  cudaError_t e;
+  {
+    LaunchTimer lt(st, "tc_prep");
+    PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
+    if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
+    k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
+    TOPS_CUDA_LAUNCH_CHECK("tc_prep");
+  }
+  {
+    LaunchTimer lt(st, "tc_scan");
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, 0, sv.D, h0, ht, sv.h};
+    if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK("tc_scan");
+  }
+  {
+    LaunchTimer lt(st, "tc_out");
+    OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 0, static_cast<bf16*>(o)};
+    if ((e = set_smem(k_out, out_smem())) != cudaSuccess) return cuda_status(e, "tc out attr");
+    const int items = s.B * NTb * s.H * (s.V / BV);
+    const int grid = items < sm_count() ? items : sm_count();
+    k_out<<<grid, 192, out_smem(), st>>>(om, op);
+    TOPS_CUDA_LAUNCH_CHECK("tc_out");
+  }
+  return TOPS_OK;
+}
+
+}  // namespace tc
+}  // namespace tops

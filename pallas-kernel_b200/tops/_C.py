@@ -35,7 +35,8 @@ class Shape(C.Structure):
 class ChunkFwdArgs(C.Structure):
     _fields_ = [("s", Shape), ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("g", C.c_void_p),
                 ("h0", C.c_void_p), ("o", C.c_void_p), ("ht", C.c_void_p), ("g_cumsum", C.c_void_p),
-                ("A", C.c_void_p), ("h", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+                ("A", C.c_void_p), ("h", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+                ("saved", C.c_void_p), ("saved_bytes", C.c_size_t)]
 
 
 class ChunkBwdArgs(C.Structure):
@@ -43,7 +44,7 @@ class ChunkBwdArgs(C.Structure):
                 ("h0", C.c_void_p), ("do_", C.c_void_p), ("dht", C.c_void_p), ("g_cumsum", C.c_void_p),
                 ("A", C.c_void_p), ("h", C.c_void_p), ("dq", C.c_void_p), ("dk", C.c_void_p), ("dv", C.c_void_p),
                 ("dg", C.c_void_p), ("dh0", C.c_void_p), ("workspace", C.c_void_p),
-                ("workspace_bytes", C.c_size_t)]
+                ("workspace_bytes", C.c_size_t), ("saved", C.c_void_p), ("saved_bytes", C.c_size_t)]
 
 
 class RecArgs(C.Structure):
@@ -72,6 +73,7 @@ SIGNATURES = {
     "tops_gla_num_chunks": (I32, [I32, I32, I32, VP, I32, VP]),
     "tops_gla_chunk_fwd": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
     "tops_gla_chunk_fwd_workspace_size": (C.c_size_t, [C.POINTER(ChunkFwdArgs)]),
+    "tops_gla_chunk_saved_size": (C.c_size_t, [C.POINTER(Shape)]),
     "tops_gla_chunk_bwd": (C.c_int, [C.POINTER(ChunkBwdArgs), VP]),
     "tops_gla_chunk_fwd_noalloc": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
     "tops_gla_chunk_bwd_workspace_size": (C.c_size_t, [C.POINTER(ChunkBwdArgs)]),

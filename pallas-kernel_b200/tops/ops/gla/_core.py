@@ -91,25 +91,39 @@ def _ws(nbytes: int, dev) -> torch.Tensor | None:
 # fused forward / backward
 # ---------------------------------------------------------------------------
 
+def saved_size(p: Plan, g) -> int:
+    """Bytes of the tensor-core path's saved block (0 when the problem runs on CUDA cores)."""
+    if g is None:
+        return 0
+    s = p.shape()
+    return int(_C.lib().tops_gla_chunk_saved_size(s))
+
+
 def chunk_fwd(p: Plan, q, k, v, g, h0, output_final_state: bool, save: bool):
-    """-> o, ht|None, (g_cumsum, A, h) when ``save`` else None."""
+    """-> o, ht|None, saved; saved = {"block": uint8 tensor} (tensor-core path) or
+    {"g_cumsum", "A", "h"} (CUDA-core path) when ``save`` else None."""
     dev = q.device
     o = torch.empty(p.B, p.T, p.H, p.V, dtype=q.dtype, device=dev)
     ht = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if output_final_state else None
-    gc = A = h = None
-    if save:
+    gc = A = h = blk = None
+    nblk = saved_size(p, g)
+    if save and nblk:
+        blk = torch.empty(nblk, dtype=torch.uint8, device=dev)
+    elif save:
         gc = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
         A = torch.empty(p.B, p.T, p.H, p.C, dtype=torch.float32, device=dev)
         h = torch.empty(p.NT, p.H, p.K, p.V, dtype=torch.float32, device=dev)
     a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(o), _C.ptr(ht),
-                        _C.ptr(gc), _C.ptr(A), _C.ptr(h), None, 0)
+                        _C.ptr(gc), _C.ptr(A), _C.ptr(h), None, 0, _C.ptr(blk), 0 if blk is None else blk.numel())
     ws = _ws(_C.lib().tops_gla_chunk_fwd_workspace_size(a), dev)
     a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
     _C.call("tops_gla_chunk_fwd", a, _C.stream_of(q))
-    return o, ht, ((gc, A, h) if save else None)
+    if not save:
+        return o, ht, None
+    return o, ht, ({"block": blk} if blk is not None else {"g_cumsum": gc, "A": A, "h": h})
 
 
-def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh0: bool = False):
+def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh0: bool = False, block=None):
     dev = q.device
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
@@ -118,7 +132,7 @@ def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh
     dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_dh0 else None
     a = _C.ChunkBwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(do), _C.ptr(dht),
                         _C.ptr(gc), _C.ptr(A), _C.ptr(h), _C.ptr(dq), _C.ptr(dk), _C.ptr(dv), _C.ptr(dg),
-                        _C.ptr(dh0), None, 0)
+                        _C.ptr(dh0), None, 0, _C.ptr(block), 0 if block is None else block.numel())
     ws = _ws(_C.lib().tops_gla_chunk_bwd_workspace_size(a), dev)
     a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
     _C.call("tops_gla_chunk_bwd", a, _C.stream_of(q))

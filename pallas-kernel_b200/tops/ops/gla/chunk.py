@@ -74,8 +74,8 @@ class _ChunkGLA(torch.autograd.Function):
         save = any(ctx.needs_input_grad[:6])
         o, ht, saved = _core.chunk_fwd(p, q, k, v, gg, h0c, output_final_state, save)
         if save:
-            gc, A, h = saved
-            ctx.save_for_backward(q, k, v, gg, h0c, gc, A, h)
+            ctx.save_for_backward(q, k, v, gg, h0c, saved.get("g_cumsum"), saved.get("A"), saved.get("h"),
+                                  saved.get("block"))
             ctx.plan = p
             ctx.g_shape = None if g is not None else (g_gamma.shape if g_gamma is not None else None)
             ctx.g_dtype = g.dtype if g is not None else (g_gamma.dtype if g_gamma is not None else None)
@@ -85,12 +85,12 @@ class _ChunkGLA(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, dht=None):
-        q, k, v, gg, h0c, gc, A, h = ctx.saved_tensors
+        q, k, v, gg, h0c, gc, A, h, blk = ctx.saved_tensors
         p = ctx.plan
         do = do.contiguous().to(q.dtype)
         dht = None if dht is None else dht.float().contiguous()
         want_dh0 = h0c is not None
-        dq, dk, dv, dg, dh0 = _core.chunk_bwd(p, q, k, v, gg, h0c, do, dht, gc, A, h, want_dh0)
+        dq, dk, dv, dg, dh0 = _core.chunk_bwd(p, q, k, v, gg, h0c, do, dht, gc, A, h, want_dh0, block=blk)
         d_g = d_gamma = None
         if ctx.needs_input_grad[3]:
             d_g = dg.to(ctx.g_dtype)
@@ -162,8 +162,10 @@ def chunk_gla_fwd(q, k, v, g, g_gamma, g_cumsum, scale, initial_state, output_fi
         A = _core.intra(p, q, k, gc, causal=True)
         o = _core.fwd_o(p, q, v, gc, A, h)
     else:
-        o, ht, (gc, A, h) = _core.chunk_fwd(p, q, k, v, gg, _f32("initial_state", initial_state),
-                                            bool(output_final_state), save=True)
+        gc = _core.cumsum(p, gg) if gg is not None else torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+        h, ht = _core.fwd_h(p, k, v, gc, _f32("initial_state", initial_state), True, bool(output_final_state))
+        A = _core.intra(p, q, k, gc, causal=True)
+        o = _core.fwd_o(p, q, v, gc, A, h)
     h = h.view(1 if p.cu_host is not None else p.B, -1, p.H, p.K, p.V).to(k.dtype)
     return gc, A, h, (ht if output_final_state else None), o
 

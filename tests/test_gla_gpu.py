@@ -352,3 +352,36 @@ def test_decode_general_shapes(gla):
             assert_close("o", o, o_r, **FP32)
             if want_ht:
                 assert_close("ht", ht, ht_r, **FP32)
+
+
+# ---------------------------------------------------------------------------
+# tensor-core (tcgen05) path: bf16, K in {128, 256}, V % 128 == 0, fixed length
+# ---------------------------------------------------------------------------
+
+TC_CASES = [
+    dict(B=2, T=640, H=2, K=256, V=512, seed=41),
+    dict(B=1, T=333, H=3, K=128, V=256, seed=42, h0=True),
+    dict(B=3, T=129, H=1, K=256, V=128, seed=43, h0=True),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=lambda c: f"B{c['B']}T{c['T']}H{c['H']}K{c['K']}V{c['V']}")
+def test_tc_forward_vs_oracle(gla, case):
+    from tops import _C
+    from tops.ops.gla import _core
+    rng = np.random.default_rng(case["seed"])
+    B, T, H, K, V = case["B"], case["T"], case["H"], case["K"], case["V"]
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32) if case.get("h0") else None
+    bf = torch.bfloat16
+    qt, kt, vt = (dev(x, bf) for x in (q, k, v))
+    p = _core.make_plan(qt, V, 64, None, K ** -0.5)
+    assert _core.saved_size(p, dev(g)) > 0, "case should take the tensor-core path"
+    o, ht = gla.chunk_gla(qt, kt, vt, dev(g), initial_state=dev(h0), output_final_state=True, chunk_size=64)
+    o_r, ht_r = O.chunk_gla(q, k, v, g, initial_state=h0, output_final_state=True, chunk_size=64)
+    assert_rel_l2("o", o, o_r, BF16_L2)
+    assert_rel_l2("ht", ht, ht_r, BF16_L2)
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
