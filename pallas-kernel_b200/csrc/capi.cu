@@ -122,6 +122,10 @@ size_t saved_bytes(const tops_gla_shape& s);
 int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
         void* o, float* ht, void* saved, cudaStream_t st);
 int read_device_error();
+size_t bwd_workspace(const tops_gla_shape& s, bool have_saved);
+int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        const void* dO, const float* dht, const void* saved, void* dq, void* dk, void* dv, float* dg, float* dh0,
+        void* workspace, cudaStream_t st);
 }  // namespace tc
 
 namespace seqpar {
@@ -198,12 +202,32 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
 // ---------------------------------------------------------------------------
 // backward
 // ---------------------------------------------------------------------------
+static bool use_tc_bwd(const tops_gla_chunk_bwd_args* a) {
+  return a->g != nullptr && a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
+}
+
 static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t* ws_need) {
   int rc = check_shape(a ? &a->s : nullptr);
   if (rc) return rc;
   const tops_gla_shape& s = a->s;
-  if ((rc = check_simt_chunk(s))) return rc;
   const bool dry = ws_need != nullptr;
+  if (use_tc_bwd(a)) {
+    const bool have = a->saved != nullptr;
+    if (have && a->saved_bytes < tc::saved_bytes(s))
+      return fail(TOPS_ERR_WORKSPACE, "chunk_bwd: saved block smaller than tops_gla_chunk_saved_size()");
+    const size_t need = tc::bwd_workspace(s, have);
+    if (dry) {
+      *ws_need = need;
+      return TOPS_OK;
+    }
+    TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && a->dq && a->dk && a->dv && a->dg,
+                   "chunk_bwd: q, k, v, do, dq, dk, dv and dg are required");
+    if (a->workspace == nullptr || a->workspace_bytes < need)
+      return fail(TOPS_ERR_WORKSPACE, "chunk_bwd: workspace smaller than tops_gla_chunk_bwd_workspace_size()");
+    return tc::bwd(s, a->q, a->k, a->v, a->g, a->h0, a->do_, a->dht, a->saved, a->dq, a->dk, a->dv, a->dg, a->dh0,
+                   a->workspace, S(stream));
+  }
+  if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {
     TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && a->dq && a->dk && a->dv && a->dg,
                    "chunk_bwd: q, k, v, do, dq, dk, dv and dg are required");

@@ -546,6 +546,313 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
   if (warp == 0) ptx::tmem_dealloc(tacc, 256);
 }
 
+// ===========================================================================
+// k_dqk: dq, dk, dg of one (batch, chunk, head, 128-wide K tile).  grid (K/128, NTb, B*H), 256 threads.
+//   dA      = scale tril(do v^T)                            (M1, contraction over V)
+//   dqi     = do h_c^T            dki = v dh_c^T            (M2, M3, contraction over V)
+//   dq      = e^{G-Gm} (dA ktil) + scale e^{G} dqi          (M4: dA x ktil, ktil = k e^{Gm-G})
+//   dk      = e^{Gm-G} (dA^T qtil) + e^{GL-G} dki           (M5: dA^T x qtil, qtil = q e^{G-Gm})
+//   dg      = revcumsum_t(q dq - k dk) + e^{GL} sum_v(h_c dh_c) + sum_t(e^{GL-G} dki k)
+// (reference chunk_gla_bwd_fused_kernel tops/ops/gla/chunk.py:1423-1479 and the
+//  _ref functions :504-743).  V is streamed in 64-wide blocks through a 2-stage
+//  TMA ring; the ring is reused afterwards for qtil, ktil and the bf16 dA.
+// ===========================================================================
+struct DqkParams {
+  int B, T, H, K, V, NTb;
+  float scale;
+  const bf16* q; const bf16* k;
+  bf16* dq; bf16* dk; float* dg;
+};
+
+struct DqkMaps {
+  CUtensorMap dO, v;   // [B,T,H,V] box (64,1,128,1)
+  CUtensorMap hs, dhs; // [B*NTb*H, K, V] box (64,128,1)
+  CUtensorMap g;       // [B,T,H,K] fp32 box (32,1,128,1)
+  CUtensorMap q, k;    // [B,T,H,K] bf16 box (64,1,128,1)
+};
+
+__global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps maps, DqkParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr uint32_t STG = 4 * TILE_BYTES;  // do, v, h, dh tiles of one V block
+  unsigned char* ring = smem;               // 2 stages
+  unsigned char* Gs = smem + 2 * STG;       // 4 x [128][32] fp32 (G, then dg_raw)
+  unsigned char* qtl = ring;                // after the V loop: qtil (2 tiles), ktil (2 tiles), dA (2 tiles)
+  unsigned char* ktl = ring + 2 * TILE_BYTES;
+  unsigned char* dAs = ring + 4 * TILE_BYTES;
+  __shared__ float GLs[128], Gms[128], part[2][128], hdh2[2][128], colsum[4][128];
+  __shared__ __align__(8) uint64_t full[2], empty[2], bar_g, bar_qk, bar_mma;
+  __shared__ uint32_t tmem_base;
+
+  const int kt = blockIdx.x, c = blockIdx.y, b = blockIdx.z / p.H, h = blockIdx.z % p.H;
+  const int k0 = kt * 128, row0 = c * BT;
+  const int srow = (b * p.NTb + c) * p.H + h;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nvb = p.V / 64;
+
+  if (warp == 0) {
+    ptx::tmem_alloc(&tmem_base, 512);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    ptx::mbar_init(&bar_g, 1);
+    ptx::mbar_init(&bar_qk, 1);
+    ptx::mbar_init(&bar_mma, 1);
+    ptx::fence_mbar_init();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tM1 = tmem_base, tM2 = tmem_base + 128, tM3 = tmem_base + 256, tM5 = tmem_base + 384;
+
+  auto issue_v = [&](int vb) {
+    const int s = vb & 1;
+    unsigned char* st = ring + s * STG;
+    ptx::mbar_arrive_expect_tx(&full[s], STG);
+    ptx::tma_load_4d(st, &maps.dO, vb * 64, h, row0, b, &full[s]);
+    ptx::tma_load_4d(st + TILE_BYTES, &maps.v, vb * 64, h, row0, b, &full[s]);
+    ptx::tma_load_3d(st + 2 * TILE_BYTES, &maps.hs, vb * 64, k0, srow, &full[s]);
+    ptx::tma_load_3d(st + 3 * TILE_BYTES, &maps.dhs, vb * 64, k0, srow, &full[s]);
+  };
+  if (tid == 0) {
+    ptx::mbar_arrive_expect_tx(&bar_g, 4 * TILE_BYTES);
+    for (int j = 0; j < 4; ++j) ptx::tma_load_4d(Gs + j * TILE_BYTES, &maps.g, k0 + 32 * j, h, row0, b, &bar_g);
+    issue_v(0);
+    if (nvb > 1) issue_v(1);
+  }
+  // ---- G = chunk-local cumsum of g (in place), GL and Gm per column ----
+  bool ok = ptx::mbar_wait(&bar_g, 0);
+  const int gcol = tid & 127, ghalf = tid >> 7;
+  unsigned char* gtile = Gs + (gcol >> 5) * TILE_BYTES;
+  const uint32_t gby = (uint32_t)(gcol & 31) * 4;
+  if (ok) {
+    float sacc = 0.f;
+    for (int r = ghalf * 64; r < ghalf * 64 + 64; ++r) sacc += *reinterpret_cast<float*>(gtile + ptx::sw128(r, gby));
+    part[ghalf][gcol] = sacc;
+  }
+  __syncthreads();
+  if (ok) {
+    float run = ghalf ? part[0][gcol] : 0.f;
+    for (int r = ghalf * 64; r < ghalf * 64 + 64; ++r) {
+      float* e = reinterpret_cast<float*>(gtile + ptx::sw128(r, gby));
+      run += *e;
+      *e = run;
+    }
+    if (ghalf == 0) Gms[gcol] = run;  // G at row 63
+    else GLs[gcol] = run;             // G at row 127
+  }
+  // ---- V loop: M1 += do v^T, M2 += do h^T, M3 += v dh^T; sum_v h*dh ----
+  const int hr = tid & 127, hh = tid >> 7;  // state row, half of the 64-wide V block
+  float my_hdh = 0.f;
+  constexpr uint32_t ID_KK = ptx::idesc_bf16(128, 128, false, false);
+  for (int vb = 0; vb < nvb && ok; ++vb) {
+    const int s = vb & 1;
+    ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
+    if (!ok) break;
+    const unsigned char* st = ring + s * STG;
+    const unsigned char* t_do = st;
+    const unsigned char* t_v = st + TILE_BYTES;
+    const unsigned char* t_h = st + 2 * TILE_BYTES;
+    const unsigned char* t_dh = st + 3 * TILE_BYTES;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t by = (uint32_t)(hh * 64 + u * 16);
+      const uint4 a = *reinterpret_cast<const uint4*>(t_h + ptx::sw128(hr, by));
+      const uint4 d = *reinterpret_cast<const uint4*>(t_dh + ptx::sw128(hr, by));
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 af = __bfloat1622float2(a2[e]), df = __bfloat1622float2(d2[e]);
+        my_hdh = fmaf(af.x, df.x, fmaf(af.y, df.y, my_hdh));
+      }
+    }
+    ptx::tc_fence_before();
+    __syncthreads();  // everyone has read h/dh of this stage (and G is complete)
+    if (tid == 0) {
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t acc = (vb | ks) ? 1u : 0u;
+        ptx::mma_bf16_ss(tM1, desc_kmajor(t_do, ks * 32), desc_kmajor(t_v, ks * 32), ID_KK, acc);
+        ptx::mma_bf16_ss(tM2, desc_kmajor(t_do, ks * 32), desc_kmajor(t_h, ks * 32), ID_KK, acc);
+        ptx::mma_bf16_ss(tM3, desc_kmajor(t_v, ks * 32), desc_kmajor(t_dh, ks * 32), ID_KK, acc);
+      }
+      ptx::mma_commit(&empty[s]);
+      if (vb + 2 < nvb) {
+        ok = ptx::mbar_wait(&empty[s], (uint32_t)((vb >> 1) & 1));
+        if (ok) issue_v(vb + 2);
+      }
+    }
+  }
+  hdh2[hh][hr] = my_hdh;
+  // all V-loop MMAs complete -> ring free
+  if (tid == 0 && ok) {
+    ptx::mma_commit(&bar_mma);
+  }
+  if (ok) ok = ptx::mbar_wait(&bar_mma, 0);
+  ptx::tc_fence_after();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    ptx::mbar_arrive_expect_tx(&bar_qk, 4 * TILE_BYTES);
+    ptx::tma_load_4d(qtl, &maps.q, k0, h, row0, b, &bar_qk);
+    ptx::tma_load_4d(qtl + TILE_BYTES, &maps.q, k0 + 64, h, row0, b, &bar_qk);
+    ptx::tma_load_4d(ktl, &maps.k, k0, h, row0, b, &bar_qk);
+    ptx::tma_load_4d(ktl + TILE_BYTES, &maps.k, k0 + 64, h, row0, b, &bar_qk);
+  }
+  // ---- dA = scale tril(M1) -> bf16 [i][j] (2 tiles) ----
+  const int qd = warp & 3, ch = warp >> 2;
+  const int i = qd * 32 + lane;
+  if (ok) {
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+      float r[32];
+      ptx::tmem_ld32(tmem_lane_addr(tM1, qd * 32, ch * 64 + cb * 32), r);
+      ptx::tmem_ld_wait();
+      unsigned char* stg = dAs + ch * TILE_BYTES;
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j0 = ch * 64 + cb * 32 + j4 * 8 + 2 * u;
+          w[u] = ptx::pack_bf16((j0 <= i) ? r[j4 * 8 + 2 * u] * p.scale : 0.f,
+                                (j0 + 1 <= i) ? r[j4 * 8 + 2 * u + 1] * p.scale : 0.f);
+        }
+        *reinterpret_cast<uint4*>(stg + ptx::sw128(i, (cb * 32 + j4 * 8) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  // ---- qtil = q e^{G-Gm}, ktil = k e^{Gm-G} in place ----
+  if (ok) ok = ptx::mbar_wait(&bar_qk, 0);
+  if (ok) {
+    // thread: row r = tid & 127, 64 columns of half (tid >> 7)
+    const int r = tid & 127, hf = tid >> 7;
+    unsigned char* qtile = qtl + hf * TILE_BYTES;
+    unsigned char* ktile = ktl + hf * TILE_BYTES;
+    for (int cc = 0; cc < 64; ++cc) {
+      const int col = hf * 64 + cc;
+      const float G = *reinterpret_cast<const float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(r, (col & 31) * 4));
+      const float x = G - Gms[col];
+      st_bf(qtile, r, cc, bf(qtile, r, cc) * __expf(x));
+      st_bf(ktile, r, cc, bf(ktile, r, cc) * __expf(-x));
+    }
+  }
+  ptx::fence_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    ptx::tc_fence_after();
+    const uint32_t ID_KM = ptx::idesc_bf16(128, 128, false, true);
+    const uint32_t ID_MM = ptx::idesc_bf16(128, 128, true, true);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      // M4 (into M1's columns): dA[i][j] x ktil[j][k]
+      ptx::mma_bf16_ss(tM1, desc_kmajor(dAs + (ks >> 2) * TILE_BYTES, (ks & 3) * 32),
+                       desc_mnmajor(ktl, ks * 2048, TILE_BYTES), ID_KM, ks ? 1u : 0u);
+      // M5: dA^T[j][i] x qtil[i][k]
+      ptx::mma_bf16_ss(tM5, desc_mnmajor(dAs, ks * 2048, TILE_BYTES), desc_mnmajor(qtl, ks * 2048, TILE_BYTES),
+                       ID_MM, ks ? 1u : 0u);
+    }
+    ptx::mma_commit(&bar_mma);
+  }
+  if (ok) ok = ptx::mbar_wait(&bar_mma, 1);
+  ptx::tc_fence_after();
+  // ---- epilogue: dq, dk (global), dg_raw (in place of G), column sums of e^{GL-G} dki k ----
+  const int row = row0 + i;
+  const bool in = row < p.T;
+  const size_t gbase = ((size_t)(b * p.T + (in ? row : 0)) * p.H + h) * p.K + k0;
+  if (ok) {
+    for (int g16 = 0; g16 < 4; ++g16) {
+      const int cb = ch * 64 + g16 * 16;  // first column of this group
+      float m4[16], m5[16], m2[16], m3[16];
+      ptx::tmem_ld16(tmem_lane_addr(tM1, qd * 32, cb), m4);
+      ptx::tmem_ld16(tmem_lane_addr(tM5, qd * 32, cb), m5);
+      ptx::tmem_ld16(tmem_lane_addr(tM2, qd * 32, cb), m2);
+      ptx::tmem_ld16(tmem_lane_addr(tM3, qd * 32, cb), m3);
+      ptx::tmem_ld_wait();
+      float qv[16], kv[16];
+      if (in) {
+        const uint4* qp = reinterpret_cast<const uint4*>(p.q + gbase + cb);
+        const uint4* kp = reinterpret_cast<const uint4*>(p.k + gbase + cb);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint4 a = qp[u], d = kp[u];
+          const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+          const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 af = __bfloat1622float2(a2[e]), df = __bfloat1622float2(d2[e]);
+            qv[u * 8 + 2 * e] = af.x; qv[u * 8 + 2 * e + 1] = af.y;
+            kv[u * 8 + 2 * e] = df.x; kv[u * 8 + 2 * e + 1] = df.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) qv[e] = kv[e] = 0.f;
+      }
+      uint32_t dqw[8], dkw[8];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int col = cb + e;
+        float* gp = reinterpret_cast<float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(i, (col & 31) * 4));
+        const float G = *gp;
+        const float x = G - Gms[col];
+        const float dq = __expf(x) * m4[e] + p.scale * __expf(G) * m2[e];
+        const float dki = __expf(GLs[col] - G) * m3[e];
+        const float dk = __expf(-x) * m5[e] + dki;
+        *gp = qv[e] * dq - kv[e] * dk;  // dg_raw
+        float cs = dki * kv[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+        if (lane == 0) colsum[qd][col] = cs;
+        m4[e] = dq;
+        m5[e] = dk;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        dqw[u] = ptx::pack_bf16(m4[2 * u], m4[2 * u + 1]);
+        dkw[u] = ptx::pack_bf16(m5[2 * u], m5[2 * u + 1]);
+      }
+      if (in) {
+        uint4* dqp = reinterpret_cast<uint4*>(p.dq + gbase + cb);
+        uint4* dkp = reinterpret_cast<uint4*>(p.dk + gbase + cb);
+        dqp[0] = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
+        dqp[1] = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
+        dkp[0] = make_uint4(dkw[0], dkw[1], dkw[2], dkw[3]);
+        dkp[1] = make_uint4(dkw[4], dkw[5], dkw[6], dkw[7]);
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  // ---- dg = reverse cumsum over rows + inter term, one thread per column ----
+  if (ok && tid < 128) {
+    const int col = tid;
+    const float inter = __expf(GLs[col]) * (hdh2[0][col] + hdh2[1][col]) + colsum[0][col] + colsum[1][col] +
+                        colsum[2][col] + colsum[3][col];
+    unsigned char* gt = Gs + (col >> 5) * TILE_BYTES;
+    const uint32_t by = (uint32_t)(col & 31) * 4;
+    float run = 0.f;
+    for (int r = 127; r >= 0; --r) {
+      run += *reinterpret_cast<const float*>(gt + ptx::sw128(r, by));
+      if (row0 + r < p.T) p.dg[((size_t)(b * p.T + row0 + r) * p.H + h) * p.K + k0 + col] = run + inter;
+    }
+  }
+  if (!ok && tid == 0) {  // drain loads that may still be in flight
+    ptx::mbar_wait(&full[0], 0);
+    ptx::mbar_wait(&full[1], 0);
+    ptx::mbar_wait(&bar_qk, 0);
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
+}
+
 TOPS_DEVICE_ERROR_READER(read_device_error)
 
 // ---------------------------------------------------------------------------
@@ -645,6 +952,75 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     const int grid = items < sm_count() ? items : sm_count();
     k_out<<<grid, 192, out_smem(), st>>>(om, op);
     TOPS_CUDA_LAUNCH_CHECK("tc_out");
+  }
+  return TOPS_OK;
+}
+
+static size_t dqk_smem() { return 2 * 4 * (size_t)TILE_BYTES + 4 * (size_t)TILE_BYTES + 1024; }
+
+size_t bwd_workspace(const tops_gla_shape& s, bool have_saved) {
+  const int NTb = (s.T + BT - 1) / BT;
+  size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);  // dh states
+  if (!have_saved) n += saved_bytes(s);
+  return n;
+}
+
+// Backward: dq, dk, dv (bf16), dg (fp32), dh0 (fp32, optional) from the forward's saved block.
+int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        const void* dO, const float* dht, const void* saved_in, void* dq, void* dk, void* dv, float* dg, float* dh0,
+        void* workspace, cudaStream_t st) {
+  const int NTb = (s.T + BT - 1) / BT;
+  char* ws = static_cast<char*>(workspace);
+  bf16* dhs = reinterpret_cast<bf16*>(ws);
+  const size_t dh_bytes = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
+  void* saved = const_cast<void*>(saved_in);
+  int rc;
+  if (saved == nullptr) {  // recompute the forward intermediates (o is discarded into dv's buffer)
+    saved = ws + dh_bytes;
+    if ((rc = fwd(s, q, k, v, g, h0, dv, nullptr, saved, st))) return rc;
+  }
+  Saved sv;
+  carve_saved(s, saved, &sv);
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  ScanMaps sm;
+  bool okm = map_tok(&sm.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+             map_tok(&sm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  OutMaps om;
+  okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) && map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
+        map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64);
+  DqkMaps dm;
+  okm = okm && map_tok(&dm.dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+        map_tok(&dm.v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+        map_state(&dm.hs, sv.h, s.B * NTb * s.H, s.K, s.V, 128) &&
+        map_state(&dm.dhs, dhs, s.B * NTb * s.H, s.K, s.V, 128) &&
+        map_tok(&dm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_tok(&dm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
+  if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
+  cudaError_t e;
+  {
+    LaunchTimer lt(st, "tc_scan_bwd");
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, 1, sv.D, dht, dh0, dhs};
+    if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK("tc_scan_bwd");
+  }
+  {
+    LaunchTimer lt(st, "tc_out_dv");
+    OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 1, static_cast<bf16*>(dv)};
+    if ((e = set_smem(k_out, out_smem())) != cudaSuccess) return cuda_status(e, "tc out attr");
+    const int items = s.B * NTb * s.H * (s.V / BV);
+    const int grid = items < sm_count() ? items : sm_count();
+    k_out<<<grid, 192, out_smem(), st>>>(om, op);
+    TOPS_CUDA_LAUNCH_CHECK("tc_out_dv");
+  }
+  {
+    LaunchTimer lt(st, "tc_dqk");
+    DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<const bf16*>(q), static_cast<const bf16*>(k),
+                 static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
+    if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
+    k_dqk<<<dim3(s.K / 128, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
+    TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
   }
   return TOPS_OK;
 }

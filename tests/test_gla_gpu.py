@@ -385,3 +385,34 @@ def test_tc_forward_vs_oracle(gla, case):
     assert_rel_l2("ht", ht, ht_r, BF16_L2)
     torch.cuda.synchronize()
     assert _C.lib().tops_gla_device_error() == 0
+
+
+@pytest.mark.parametrize("case", TC_CASES + [dict(B=1, T=200, H=2, K=128, V=128, seed=44, h0=True, dht=True)],
+                         ids=lambda c: f"B{c['B']}T{c['T']}H{c['H']}K{c['K']}V{c['V']}")
+def test_tc_backward_vs_oracle(gla, case):
+    """bf16 fwd+bwd on the tensor-core path through torch.autograd vs the fp64 oracle (rel-L2 2e-2)."""
+    from tops import _C
+    rng = np.random.default_rng(case["seed"] + 100)
+    B, T, H, K, V = case["B"], case["T"], case["H"], case["K"], case["V"]
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    do = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32) if case.get("h0") else None
+    dht = rng.standard_normal((B, H, K, V), dtype=np.float32) if case.get("dht") else None
+    bf = torch.bfloat16
+    qt, kt, vt = (dev(x, bf).requires_grad_() for x in (q, k, v))
+    gt = dev(g).requires_grad_()
+    h0t = dev(h0)
+    if h0t is not None:
+        h0t.requires_grad_()
+    o, ht = gla.chunk_gla(qt, kt, vt, gt, initial_state=h0t, output_final_state=True, chunk_size=64)
+    loss = (o.float() * dev(do)).sum() + (0 if dht is None else (ht * dev(dht)).sum())
+    loss.backward()
+    dq_r, dk_r, dv_r, dg_r, dh0_r = O.chunk_gla_bwd(q, k, v, g, None, K ** -0.5, h0, None, None, do, dht, None, 64)
+    for nm, got, want in (("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r), ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r)):
+        assert_rel_l2(nm, got, want, BF16_L2)
+    if h0t is not None:
+        assert_rel_l2("dh0", h0t.grad, dh0_r, BF16_L2)
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
