@@ -47,16 +47,22 @@ def peaks():
     return dict(hbm_gbs=6650.0, bf16=1590.0, bf16_sustained=1400.0, source="fallback")
 
 
-# algorithmic work per token per head (dense C x C tiles, no recompute) -- per kernel
-def kernel_flops(name, K, V, C):
+# Algorithmic work of each kernel per token per head: (flops, bytes).  Flops count
+# dense BT x BT intra-chunk tiles (BT = 128 on the tensor-core path); bytes count
+# every tensor the kernel must read or write once (bf16 = 2 B, fp32 = 4 B), including
+# the per-chunk states h / dh (K*V bf16 per 128 tokens) that the kernels exchange.
+def kernel_work(name, K, V, BT=128):
+    st = 2 * K * V / BT  # one bf16 chunk state per BT tokens
     return {
-        "chunk_fwd_h": 2 * K * V, "chunk_fwd_intra": 2 * C * K, "chunk_fwd_o": 2 * K * V + 2 * C * V,
-        "chunk_bwd_dh": 2 * K * V, "chunk_bwd_dA": 2 * C * V, "chunk_bwd_dv": 2 * C * V + 2 * K * V,
-        "chunk_bwd_dqk_intra": 4 * C * K, "chunk_bwd_dqkg": 4 * K * V,
-        "tc_chunk_fwd": 4 * K * V + 2 * C * (K + V),
-        "tc_chunk_bwd_dh": 2 * K * V + 2 * C * V + 2 * K * V,
-        "tc_chunk_bwd_dqkg": 2 * C * V + 4 * C * K + 4 * K * V,
-    }.get(name)
+        "tc_prep": (2 * BT * K, 2 * K + 2 * K + 4 * K + 2 * K + 2 * K + 2 * BT),
+        "tc_scan": (2 * K * V, 2 * K + 2 * V + st),
+        "tc_out": (2 * K * V + 2 * BT * V, 2 * K + 2 * BT + st + 2 * V + 2 * V),
+        "tc_scan_bwd": (2 * K * V, 2 * K + 2 * V + st),
+        "tc_out_dv": (2 * K * V + 2 * BT * V, 2 * K + 2 * BT + st + 2 * V + 2 * V),
+        "tc_dqk": (2 * BT * V + 4 * K * V + 4 * BT * K,
+                   2 * V + 2 * V + 2 * st + 2 * K + 2 * K + 4 * K + 2 * K + 2 * K + 4 * K),
+        "recurrent_decode": (None, None),
+    }.get(name, (None, None))
 
 
 def fwd_bwd_flops_per_token_head(K, V, C):
@@ -289,6 +295,14 @@ def run_ours(args):
     ms = max_over_ranks(ms, world)
     tokens = B * T * world
     value = tokens / (ms * 1e-3)
+    if args.kernels_only:
+        clk.__exit__()
+        if rank == 0:
+            print(json.dumps({"kernels_only": True, "ms_per_step": ms, "tokens_per_s": value, "B": B}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
 
     # per-kernel live timing (CUDA events around each launch on its stream)
     _C.timing_enable(True)
@@ -307,18 +321,39 @@ def run_ours(args):
     dom_name, (dom_total, dom_n) = dom
     dom_ms = dom_total / dom_n
     pk = peaks()
-    flops_tok = kernel_flops(dom_name, K, V, C)
     units = B * T * H
     kernels_share = {nm: round(v_[0] / tot, 4) for nm, v_ in sorted(per.items(), key=lambda kv: -kv[1][0])}
     traffic = None
-    tj = ROOT / "profiles" / "traffic.json"
+    tj = ROOT / "profiles" / "traffic.txt"
     if tj.exists():
-        traffic = json.loads(tj.read_text()).get(dom_name)
-    roof = {"kernel": dom_name, "bound": "tensor", "unit": "TFLOP/s",
-            "achieved": (flops_tok * units / (dom_ms * 1e-3)) / 1e12 if flops_tok else None,
-            "peak": pk["bf16_sustained"], "peak_source": f"{pk['source']} bf16 sustained (kernel timed inside a step)",
-            "traffic": traffic, "kernel_ms": dom_ms, "kernel_shares": kernels_share}
+        for line in tj.read_text().splitlines():
+            f_ = line.split()
+            if len(f_) >= 2 and not line.startswith("#") and f_[0] == dom_name:
+                traffic = float(f_[1])
+    ridge = pk["bf16_sustained"] * 1e12 / (pk["hbm_gbs"] * 1e9)
+    per_kernel = {}
+    for nm, (tt, n) in per.items():
+        f, by = kernel_work(nm, K, V)
+        if f is None:
+            continue
+        kms = tt / n
+        per_kernel[nm] = {"ms": round(kms, 5), "tflops": round(f * units / (kms * 1e-3) / 1e12, 2),
+                          "gbs": round(by * units / (kms * 1e-3) / 1e9, 1), "intensity": round(f / by, 1)}
+    f, by = kernel_work(dom_name, K, V)
+    if f is not None and f / by >= ridge:
+        roof = {"kernel": dom_name, "bound": "tensor", "unit": "TFLOP/s", "achieved": f * units / (dom_ms * 1e-3) / 1e12,
+                "peak": pk["bf16_sustained"], "peak_source": f"{pk['source']} bf16 sustained (kernel timed inside a step)"}
+    elif f is not None:
+        roof = {"kernel": dom_name, "bound": "hbm", "unit": "GB/s", "achieved": by * units / (dom_ms * 1e-3) / 1e9,
+                "peak": pk["hbm_gbs"], "peak_source": f"{pk['source']} HBM copy bandwidth"}
+    else:
+        roof = {"kernel": dom_name, "bound": "hbm", "unit": "GB/s", "achieved": None, "peak": pk["hbm_gbs"],
+                "peak_source": pk["source"]}
     roof["frac"] = roof["achieved"] / roof["peak"] if roof["achieved"] else None
+    roof.update({"traffic": traffic, "traffic_unit": "bytes per launch (ncu dram read+write)",
+                 "algorithmic_bytes_per_launch": None if by is None else by * units,
+                 "algorithmic_flops_per_launch": None if f is None else f * units,
+                 "kernel_ms": dom_ms, "kernel_shares": kernels_share, "per_kernel": per_kernel})
     step_flops = fwd_bwd_flops_per_token_head(K, V, C) * units
     step_bytes = fwd_bwd_bytes_per_token_head(K, V) * units
     step_roof = {"tflops": step_flops / (ms * 1e-3) / 1e12, "tensor_frac": step_flops / (ms * 1e-3) / 1e12 / pk["bf16"],
@@ -433,7 +468,12 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch", type=int, default=None, help="override B per GPU (profiling runs on a smaller case)")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="only the timed fwd+bwd loop (no decode / e2e / CPU legs); for ncu launch lists")
     args = ap.parse_args()
+    if args.batch is not None:
+        CFG3["B"] = int(args.batch)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
