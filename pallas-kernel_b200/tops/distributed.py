@@ -1,0 +1,165 @@
+"""Multi-GPU helpers for the GLA ops (one process per GPU, ``torch.distributed``).
+
+The reference has no multi-device code; BASELINE asks for two layouts:
+
+* **batch x heads sharding** (configs 2 and 3): the (sequence, head) units are
+  independent, so every rank runs the ops on its own slice with no collective.
+  :func:`shard` picks a rank's slice.
+
+* **sequence parallelism** (config 4): one long sequence is split into contiguous
+  spans, one per rank.  The chunked scan is linear in the incoming state
+  (tops/ops/common/chunk_h.py:372-386): a span's final state is
+  ``D * H_in + S`` with ``S`` its final state from a zero state and
+  ``D = exp(sum of its gates)`` (diagonal in K).  Each rank computes ``(S, D)``,
+  the ranks all-gather them, every rank forms its incoming state ``H_r`` by a
+  prefix over the earlier ranks, then runs the full forward with ``H_r``.  The
+  backward is the transpose: ``dH_r = D_r * dH_{r+1} + dh0_local_r``, gathered
+  and combined as a suffix.  The forward is exact (the same linear algebra the
+  single-device scan does), so concatenating the ranks' outputs equals the
+  single-device result.
+
+The compute steps are passed in as callables so that the exchange logic can be
+tested on CPU ranks (gloo) with any implementation of the local ops; the GPU
+defaults use this library's kernels.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["shard", "prefix_states", "suffix_grads", "all_gather_stack", "seq_parallel_forward",
+           "seq_parallel_backward", "chunk_gla_seq_parallel"]
+
+
+def shard(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
+    """Contiguous slice ``rank`` of ``world`` along ``dim`` (batch or heads); sizes must divide."""
+    n = x.shape[dim]
+    assert n % world == 0, f"dimension {dim} of size {n} does not split over {world} ranks"
+    s = n // world
+    return x.narrow(dim, rank * s, s)
+
+
+def all_gather_stack(x: torch.Tensor, group=None) -> torch.Tensor:
+    """[world, *x.shape] stack of every rank's ``x`` (one all-gather)."""
+    world = dist.get_world_size(group)
+    out = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(out, x.contiguous(), group=group)
+    return torch.stack(out, 0)
+
+
+def prefix_states(S: torch.Tensor, D: torch.Tensor, h0: torch.Tensor | None) -> torch.Tensor:
+    """Incoming states of every rank: H_0 = h0 (or 0), H_{r+1} = D_r * H_r + S_r.
+
+    S: [R, N, H, K, V] span final states from a zero state; D: [R, N, H, K] span decays.
+    Returns [R, N, H, K, V].
+    """
+    R = S.shape[0]
+    H = torch.zeros_like(S[0]) if h0 is None else h0.to(S.dtype).clone()
+    out = []
+    for r in range(R):
+        out.append(H)
+        H = D[r][..., None] * H + S[r]
+    return torch.stack(out, 0)
+
+
+def suffix_grads(dh0_local: torch.Tensor, D: torch.Tensor, dht: torch.Tensor | None) -> torch.Tensor:
+    """Gradient w.r.t. every rank's final state: G_{R-1} = dht (or 0), G_{r-1} = D_r * G_r + dh0_local_r.
+
+    dh0_local: [R, N, H, K, V] gradient of each span's own loss w.r.t. its incoming state
+    (computed with a zero final-state gradient); D: [R, N, H, K].  Returns [R, N, H, K, V]
+    where entry r is the final-state gradient rank r must use in its backward.
+    """
+    R = dh0_local.shape[0]
+    G = torch.zeros_like(dh0_local[0]) if dht is None else dht.to(dh0_local.dtype).clone()
+    out = [None] * R
+    for r in range(R - 1, -1, -1):
+        out[r] = G
+        G = D[r][..., None] * G + dh0_local[r]
+    return torch.stack(out, 0)
+
+
+def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, h0=None, group=None):
+    """Forward of one rank's span.
+
+    local_fwd(q, k, v, g, h0) -> (o, final_state) runs the chunked forward on this span;
+    span_decay(g) -> D [N, H, K] is exp of the span's gate sums.  ``h0`` (rank 0's initial
+    state) is read on every rank (pass the same tensor or None).  Returns (o, H_in, ht_global)
+    where H_in is this rank's incoming state and ht_global the final state of the whole
+    sequence (identical on all ranks).
+    """
+    rank = dist.get_rank(group)
+    _, S = local_fwd(q, k, v, g, None)
+    D = span_decay(g)
+    S_all = all_gather_stack(S, group)
+    D_all = all_gather_stack(D.to(S.dtype), group)
+    H_all = prefix_states(S_all, D_all, h0)
+    H_in = H_all[rank]
+    o, ht_local = local_fwd(q, k, v, g, H_in)
+    ht_global = D_all[-1][..., None] * H_all[-1] + S_all[-1]
+    return o, H_in, ht_global
+
+
+def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=None, group=None):
+    """Backward of one rank's span.
+
+    local_bwd(H_in, do, dht) -> (dq, dk, dv, dg, dh0) runs the chunked backward of this span
+    from its incoming state.  D: this span's decay [N, H, K].  ``dht`` is the gradient of the
+    whole sequence's final state (read by the last rank).  Returns (dq, dk, dv, dg, dh0) where
+    dh0 is the gradient w.r.t. this rank's incoming state (rank 0: the user's initial state).
+    """
+    rank = dist.get_rank(group)
+    *_, dh0_local = local_bwd(H_in, do, None)
+    L_all = all_gather_stack(dh0_local, group)
+    D_all = all_gather_stack(D.to(dh0_local.dtype), group)
+    G_all = suffix_grads(L_all, D_all, dht)
+    return local_bwd(H_in, do, G_all[rank])
+
+
+class _SeqParallelChunkGLA(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, h0, scale, chunk_size, group):
+        from .ops.gla import _core
+
+        p = _core.make_plan(q, v.shape[-1], chunk_size, None, scale)
+
+        def local_fwd(q_, k_, v_, g_, h_):
+            o, ht, _ = _core.chunk_fwd(p, q_, k_, v_, g_, h_, True, save=False)
+            return o, ht
+
+        o, H_in, ht = seq_parallel_forward(local_fwd, lambda g_: _core.span_decay(p, g_), q, k, v, g, h0, group)
+        ctx.save_for_backward(q, k, v, g, H_in)
+        ctx.plan, ctx.group, ctx.has_h0 = p, group, h0 is not None
+        return o, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        from .ops.gla import _core
+
+        q, k, v, g, H_in = ctx.saved_tensors
+        p = ctx.plan
+
+        def local_bwd(h_in, do_, dht_):
+            return _core.chunk_bwd(p, q, k, v, g, h_in, do_, dht_, want_dh0=True)
+
+        D = _core.span_decay(p, g)
+        dq, dk, dv, dg, dh0 = seq_parallel_backward(local_bwd, D, H_in, do.contiguous().to(q.dtype),
+                                                    None if dht is None else dht.float(), ctx.group)
+        rank = dist.get_rank(ctx.group)
+        d_h0 = dh0 if (ctx.has_h0 and rank == 0) else None
+        return dq, dk, dv, dg, d_h0, None, None, None
+
+
+def chunk_gla_seq_parallel(q, k, v, g, scale=None, initial_state=None, chunk_size=64, group=None):
+    """chunk_gla over a sequence split into contiguous spans, one per rank (differentiable).
+
+    q, k, g: this rank's span [B, T_r, H, K]; v: [B, T_r, H, V] (CUDA tensors, same T_r on
+    every rank).  initial_state: [B, H, K, V] state before rank 0's span (or None).
+    Returns (o of this span, final state of the whole sequence).  The only communication
+    is two all-gathers of [B, H, K, V] fp32 states (+ [B, H, K] decays) per direction.
+    """
+    if scale is None:
+        scale = q.shape[-1] ** -0.5
+    return _SeqParallelChunkGLA.apply(q, k, v, g.float().contiguous(), initial_state, float(scale), int(chunk_size),
+                                      group)
