@@ -256,6 +256,27 @@ TOPS_API int tops_gla_span_decay(const tops_gla_shape* s, const float* g, float*
 TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, const float* decay, const float* h_in,
                            const float* s_local, float* out, void* stream);
 
+/* ---- XLA custom calls (JAX frontend) ---------------------------------------
+ * Status-returning legacy custom-call signature used by jax custom_call lowering:
+ * (cudaStream_t, void** buffers, const char* opaque, size_t opaque_len,
+ *  XlaCustomCallStatus*).  `opaque` is a tops_gla_xla_desc; the buffer order is
+ * documented at each definition (csrc/xla_custom_call.cu).  They replace the
+ * reference's in-process pl.pallas_call launches (tops/ops/gla/chunk.py:1147-1164,
+ * tops/ops/gla/fused_recurrent.py:343-362) for JAX callers. */
+typedef struct tops_gla_xla_desc {
+  int32_t B, T, H, K, V, chunk_size, dtype;
+  float scale;
+  int32_t has_g, has_h0, out_final, has_dht, want_dh0, reverse;
+  uint64_t saved_bytes, workspace_bytes;
+} tops_gla_xla_desc;
+
+TOPS_API void tops_gla_xla_chunk_fwd(void* stream, void** buffers, const char* opaque, size_t opaque_len,
+                                     void* status);
+TOPS_API void tops_gla_xla_chunk_bwd(void* stream, void** buffers, const char* opaque, size_t opaque_len,
+                                     void* status);
+TOPS_API void tops_gla_xla_recurrent_fwd(void* stream, void** buffers, const char* opaque, size_t opaque_len,
+                                         void* status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,13 @@ class RecBwdArgs(C.Structure):
                 ("dh0", C.c_void_p)]
 
 
+class XlaDesc(C.Structure):
+    _fields_ = [("B", C.c_int32), ("T", C.c_int32), ("H", C.c_int32), ("K", C.c_int32), ("V", C.c_int32),
+                ("chunk_size", C.c_int32), ("dtype", C.c_int32), ("scale", C.c_float), ("has_g", C.c_int32),
+                ("has_h0", C.c_int32), ("out_final", C.c_int32), ("has_dht", C.c_int32), ("want_dh0", C.c_int32),
+                ("reverse", C.c_int32), ("saved_bytes", C.c_uint64), ("workspace_bytes", C.c_uint64)]
+
+
 VP, I32, F32C = C.c_void_p, C.c_int32, C.c_float
 SIGNATURES = {
     "tops_gla_last_error": (C.c_char_p, []),
@@ -93,6 +100,9 @@ SIGNATURES = {
                                           VP]),
     "tops_gla_span_decay": (C.c_int, [C.POINTER(Shape), VP, VP, VP]),
     "tops_gla_state_combine": (C.c_int, [I32, I32, I32, I32, VP, VP, VP, VP, VP]),
+    "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
+    "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
+    "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
 }
 
 _lib = None

@@ -46,6 +46,7 @@ def test_library_exports_every_declared_symbol(lib):
 def test_struct_layouts_match_ctypes(lib, tmp_path):
     """Compile a C probe against the header and compare sizeof/offsetof with ctypes."""
     structs = {"tops_gla_shape": lib.Shape, "tops_gla_chunk_fwd_args": lib.ChunkFwdArgs,
+               "tops_gla_xla_desc": lib.XlaDesc,
                "tops_gla_chunk_bwd_args": lib.ChunkBwdArgs, "tops_gla_recurrent_args": lib.RecArgs,
                "tops_gla_recurrent_bwd_args": lib.RecBwdArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
@@ -104,3 +105,10 @@ def test_workspace_queries_are_pure(lib):
     assert n >= 8 * 4096 * 4 * (256 + 64) * 4  # g_cumsum + A (fp32) at least
     b = lib.ChunkBwdArgs(s, *([None] * 15), None, 0)
     assert L.tops_gla_chunk_bwd_workspace_size(ctypes.byref(b)) > n
+
+
+def test_jax_frontend_imports_where_jax_exists():
+    """The JAX custom-call frontend needs jax (absent on this image and the B200 box)."""
+    pytest.importorskip("jax")
+    import tops.jax as TJ  # noqa: F401
+    assert callable(TJ.chunk_gla)
