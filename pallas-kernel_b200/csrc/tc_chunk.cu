@@ -550,17 +550,20 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 // k_dqk: dq, dk, dg of one (batch, chunk, head, 128-wide K tile).  grid (K/128, NTb, B*H), 256 threads.
 //   dA      = scale tril(do v^T)                            (M1, contraction over V)
 //   dqi     = do h_c^T            dki = v dh_c^T            (M2, M3, contraction over V)
-//   dq      = e^{G-Gm} (dA ktil) + scale e^{G} dqi          (M4: dA x ktil, ktil = k e^{Gm-G})
-//   dk      = e^{Gm-G} (dA^T qtil) + e^{GL-G} dki           (M5: dA^T x qtil, qtil = q e^{G-Gm})
+//   dq      = e^{G-Gm} (dA ktil + scale e^{Gm} dqi)         (M4 = dA x ktil,  ktil = k e^{Gm-G})
+//   dk      = e^{Gm-G} (dA^T qtil + e^{GL-Gm} dki)          (M5 = dA^T x qtil, qtil = q e^{G-Gm})
 //   dg      = revcumsum_t(q dq - k dk) + e^{GL} sum_v(h_c dh_c) + sum_t(e^{GL-G} dki k)
+//             with q dq = qtil (M4 + scale e^{Gm} dqi) and k dk = ktil (M5 + e^{GL-Gm} dki)
 // (reference chunk_gla_bwd_fused_kernel tops/ops/gla/chunk.py:1423-1479 and the
-//  _ref functions :504-743).  V is streamed in 64-wide blocks through a 2-stage
-//  TMA ring; the ring is reused afterwards for qtil, ktil and the bf16 dA.
+//  _ref functions :504-743).
+// Roles during the V stream: warp 0 = TMA producer, warp 1 = MMA issuer, warps 2-3 =
+// chunk-local cumsum of g (in place), warps 4-7 = sum_v h*dh.  The 2-stage operand
+// ring is released by the MMA commit plus the four reducer warps.  After the stream
+// the ring holds q -> qtil, k -> ktil (stage 0) and the bf16 dA (stage 1).
 // ===========================================================================
 struct DqkParams {
   int B, T, H, K, V, NTb;
   float scale;
-  const bf16* q; const bf16* k;
   bf16* dq; bf16* dk; float* dg;
 };
 
@@ -571,16 +574,20 @@ struct DqkMaps {
   CUtensorMap q, k;    // [B,T,H,K] bf16 box (64,1,128,1)
 };
 
+__device__ __forceinline__ float gval(const unsigned char* Gs, int row, int col) {
+  return *reinterpret_cast<const float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(row, (col & 31) * 4));
+}
+
 __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps maps, DqkParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr uint32_t STG = 4 * TILE_BYTES;  // do, v, h, dh tiles of one V block
   unsigned char* ring = smem;               // 2 stages
-  unsigned char* Gs = smem + 2 * STG;       // 4 x [128][32] fp32 (G, then dg_raw)
-  unsigned char* qtl = ring;                // after the V loop: qtil (2 tiles), ktil (2 tiles), dA (2 tiles)
+  unsigned char* Gs = smem + 2 * STG;       // 4 x [128][32] fp32: G, then dg_raw
+  unsigned char* qtl = ring;                // after the stream: qtil (2 tiles), ktil (2 tiles)
   unsigned char* ktl = ring + 2 * TILE_BYTES;
-  unsigned char* dAs = ring + 4 * TILE_BYTES;
-  __shared__ float GLs[128], Gms[128], part[2][128], hdh2[2][128], colsum[4][128];
+  unsigned char* dAs = ring + STG;          // dA bf16 (2 tiles)
+  __shared__ float GLs[128], Gms[128], eGm[128], eGLm[128], hdh2[2][128], colsum[4][128], dgtot[128];
   __shared__ __align__(8) uint64_t full[2], empty[2], bar_g, bar_qk, bar_mma;
   __shared__ uint32_t tmem_base;
 
@@ -594,10 +601,10 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
     ptx::tmem_alloc(&tmem_base, 512);
     ptx::tmem_relinquish();
   }
-  if (tid == 0) {
+  if (tid == 32) {
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 reducer warps
     }
     ptx::mbar_init(&bar_g, 1);
     ptx::mbar_init(&bar_qk, 1);
@@ -608,106 +615,118 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tM1 = tmem_base, tM2 = tmem_base + 128, tM3 = tmem_base + 256, tM5 = tmem_base + 384;
+  bool ok = true;
 
-  auto issue_v = [&](int vb) {
-    const int s = vb & 1;
-    unsigned char* st = ring + s * STG;
-    ptx::mbar_arrive_expect_tx(&full[s], STG);
-    ptx::tma_load_4d(st, &maps.dO, vb * 64, h, row0, b, &full[s]);
-    ptx::tma_load_4d(st + TILE_BYTES, &maps.v, vb * 64, h, row0, b, &full[s]);
-    ptx::tma_load_3d(st + 2 * TILE_BYTES, &maps.hs, vb * 64, k0, srow, &full[s]);
-    ptx::tma_load_3d(st + 3 * TILE_BYTES, &maps.dhs, vb * 64, k0, srow, &full[s]);
-  };
-  if (tid == 0) {
-    ptx::mbar_arrive_expect_tx(&bar_g, 4 * TILE_BYTES);
-    for (int j = 0; j < 4; ++j) ptx::tma_load_4d(Gs + j * TILE_BYTES, &maps.g, k0 + 32 * j, h, row0, b, &bar_g);
-    issue_v(0);
-    if (nvb > 1) issue_v(1);
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      ptx::mbar_arrive_expect_tx(&bar_g, 4 * TILE_BYTES);
+      for (int j = 0; j < 4; ++j) ptx::tma_load_4d(Gs + j * TILE_BYTES, &maps.g, k0 + 32 * j, h, row0, b, &bar_g);
+      for (int vb = 0; vb < nvb && ok; ++vb) {
+        const int s = vb & 1;
+        if (vb >= 2) ok = ptx::mbar_wait(&empty[s], (uint32_t)(((vb >> 1) - 1) & 1));
+        if (!ok) break;
+        unsigned char* st = ring + s * STG;
+        ptx::mbar_arrive_expect_tx(&full[s], STG);
+        ptx::tma_load_4d(st, &maps.dO, vb * 64, h, row0, b, &full[s]);
+        ptx::tma_load_4d(st + TILE_BYTES, &maps.v, vb * 64, h, row0, b, &full[s]);
+        ptx::tma_load_3d(st + 2 * TILE_BYTES, &maps.hs, vb * 64, k0, srow, &full[s]);
+        ptx::tma_load_3d(st + 3 * TILE_BYTES, &maps.dhs, vb * 64, k0, srow, &full[s]);
+      }
+      // stage 0 gets q and k once its last V block is released
+      if (ok) {
+        const int last0 = (nvb - 1) & ~1;  // last V block that used stage 0
+        ok = ptx::mbar_wait(&empty[0], (uint32_t)((last0 >> 1) & 1));
+      }
+      if (ok) {
+        ptx::mbar_arrive_expect_tx(&bar_qk, 4 * TILE_BYTES);
+        ptx::tma_load_4d(qtl, &maps.q, k0, h, row0, b, &bar_qk);
+        ptx::tma_load_4d(qtl + TILE_BYTES, &maps.q, k0 + 64, h, row0, b, &bar_qk);
+        ptx::tma_load_4d(ktl, &maps.k, k0, h, row0, b, &bar_qk);
+        ptx::tma_load_4d(ktl + TILE_BYTES, &maps.k, k0 + 64, h, row0, b, &bar_qk);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer for the V stream ----------------
+    if (lane == 0) {
+      constexpr uint32_t ID_KK = ptx::idesc_bf16(128, 128, false, false);
+      for (int vb = 0; vb < nvb && ok; ++vb) {
+        const int s = vb & 1;
+        ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const unsigned char* st = ring + s * STG;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t acc = (vb | ks) ? 1u : 0u;
+          ptx::mma_bf16_ss(tM1, desc_kmajor(st, ks * 32), desc_kmajor(st + TILE_BYTES, ks * 32), ID_KK, acc);
+          ptx::mma_bf16_ss(tM2, desc_kmajor(st, ks * 32), desc_kmajor(st + 2 * TILE_BYTES, ks * 32), ID_KK, acc);
+          ptx::mma_bf16_ss(tM3, desc_kmajor(st + TILE_BYTES, ks * 32), desc_kmajor(st + 3 * TILE_BYTES, ks * 32),
+                           ID_KK, acc);
+        }
+        ptx::mma_commit(&empty[s]);
+      }
+      if (ok) ptx::mma_commit(&bar_mma);
+    }
+  } else if (warp < 4) {
+    // ---------------- chunk-local cumsum of g, in place (2 columns per thread) ----------------
+    ok = ptx::mbar_wait(&bar_g, 0);
+    if (ok) {
+      const int c0 = (tid - 64) * 2;
+      float r0 = 0.f, r1 = 0.f;
+      for (int r = 0; r < 128; ++r) {
+        float* e0 = reinterpret_cast<float*>(Gs + (c0 >> 5) * TILE_BYTES + ptx::sw128(r, (c0 & 31) * 4));
+        const float2 x = *reinterpret_cast<float2*>(e0);
+        r0 += x.x;
+        r1 += x.y;
+        *reinterpret_cast<float2*>(e0) = make_float2(r0, r1);
+        if (r == 63) {
+          Gms[c0] = r0;
+          Gms[c0 + 1] = r1;
+        }
+      }
+      GLs[c0] = r0;
+      GLs[c0 + 1] = r1;
+      eGm[c0] = __expf(Gms[c0]);
+      eGm[c0 + 1] = __expf(Gms[c0 + 1]);
+      eGLm[c0] = __expf(r0 - Gms[c0]);
+      eGLm[c0 + 1] = __expf(r1 - Gms[c0 + 1]);
+    }
+  } else {
+    // ---------------- sum_v h*dh of the state rows, per V block ----------------
+    const int hr = (tid - 128);  // state row 0..127
+    float acc = 0.f;
+    for (int vb = 0; vb < nvb && ok; ++vb) {
+      const int s = vb & 1;
+      ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
+      if (!ok) break;
+      const unsigned char* th = ring + s * STG + 2 * TILE_BYTES;
+      const unsigned char* tdh = th + TILE_BYTES;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 a = *reinterpret_cast<const uint4*>(th + ptx::sw128(hr, u * 16));
+        const uint4 d = *reinterpret_cast<const uint4*>(tdh + ptx::sw128(hr, u * 16));
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 af = __bfloat1622float2(a2[e]), df = __bfloat1622float2(d2[e]);
+          acc = fmaf(af.x, df.x, fmaf(af.y, df.y, acc));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&empty[s]);
+    }
+    hdh2[0][hr] = acc;
   }
-  // ---- G = chunk-local cumsum of g (in place), GL and Gm per column ----
-  bool ok = ptx::mbar_wait(&bar_g, 0);
-  const int gcol = tid & 127, ghalf = tid >> 7;
-  unsigned char* gtile = Gs + (gcol >> 5) * TILE_BYTES;
-  const uint32_t gby = (uint32_t)(gcol & 31) * 4;
-  if (ok) {
-    float sacc = 0.f;
-    for (int r = ghalf * 64; r < ghalf * 64 + 64; ++r) sacc += *reinterpret_cast<float*>(gtile + ptx::sw128(r, gby));
-    part[ghalf][gcol] = sacc;
-  }
+  // ---------------- all threads: V-stream MMAs done, G done ----------------
   __syncthreads();
-  if (ok) {
-    float run = ghalf ? part[0][gcol] : 0.f;
-    for (int r = ghalf * 64; r < ghalf * 64 + 64; ++r) {
-      float* e = reinterpret_cast<float*>(gtile + ptx::sw128(r, gby));
-      run += *e;
-      *e = run;
-    }
-    if (ghalf == 0) Gms[gcol] = run;  // G at row 63
-    else GLs[gcol] = run;             // G at row 127
-  }
-  // ---- V loop: M1 += do v^T, M2 += do h^T, M3 += v dh^T; sum_v h*dh ----
-  const int hr = tid & 127, hh = tid >> 7;  // state row, half of the 64-wide V block
-  float my_hdh = 0.f;
-  constexpr uint32_t ID_KK = ptx::idesc_bf16(128, 128, false, false);
-  for (int vb = 0; vb < nvb && ok; ++vb) {
-    const int s = vb & 1;
-    ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
-    if (!ok) break;
-    const unsigned char* st = ring + s * STG;
-    const unsigned char* t_do = st;
-    const unsigned char* t_v = st + TILE_BYTES;
-    const unsigned char* t_h = st + 2 * TILE_BYTES;
-    const unsigned char* t_dh = st + 3 * TILE_BYTES;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t by = (uint32_t)(hh * 64 + u * 16);
-      const uint4 a = *reinterpret_cast<const uint4*>(t_h + ptx::sw128(hr, by));
-      const uint4 d = *reinterpret_cast<const uint4*>(t_dh + ptx::sw128(hr, by));
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 af = __bfloat1622float2(a2[e]), df = __bfloat1622float2(d2[e]);
-        my_hdh = fmaf(af.x, df.x, fmaf(af.y, df.y, my_hdh));
-      }
-    }
-    ptx::tc_fence_before();
-    __syncthreads();  // everyone has read h/dh of this stage (and G is complete)
-    if (tid == 0) {
-      ptx::tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t acc = (vb | ks) ? 1u : 0u;
-        ptx::mma_bf16_ss(tM1, desc_kmajor(t_do, ks * 32), desc_kmajor(t_v, ks * 32), ID_KK, acc);
-        ptx::mma_bf16_ss(tM2, desc_kmajor(t_do, ks * 32), desc_kmajor(t_h, ks * 32), ID_KK, acc);
-        ptx::mma_bf16_ss(tM3, desc_kmajor(t_v, ks * 32), desc_kmajor(t_dh, ks * 32), ID_KK, acc);
-      }
-      ptx::mma_commit(&empty[s]);
-      if (vb + 2 < nvb) {
-        ok = ptx::mbar_wait(&empty[s], (uint32_t)((vb >> 1) & 1));
-        if (ok) issue_v(vb + 2);
-      }
-    }
-  }
-  hdh2[hh][hr] = my_hdh;
-  // all V-loop MMAs complete -> ring free
-  if (tid == 0 && ok) {
-    ptx::mma_commit(&bar_mma);
-  }
   if (ok) ok = ptx::mbar_wait(&bar_mma, 0);
   ptx::tc_fence_after();
-  __syncthreads();
-  if (tid == 0 && ok) {
-    ptx::mbar_arrive_expect_tx(&bar_qk, 4 * TILE_BYTES);
-    ptx::tma_load_4d(qtl, &maps.q, k0, h, row0, b, &bar_qk);
-    ptx::tma_load_4d(qtl + TILE_BYTES, &maps.q, k0 + 64, h, row0, b, &bar_qk);
-    ptx::tma_load_4d(ktl, &maps.k, k0, h, row0, b, &bar_qk);
-    ptx::tma_load_4d(ktl + TILE_BYTES, &maps.k, k0 + 64, h, row0, b, &bar_qk);
-  }
-  // ---- dA = scale tril(M1) -> bf16 [i][j] (2 tiles) ----
   const int qd = warp & 3, ch = warp >> 2;
-  const int i = qd * 32 + lane;
+  const int i = qd * 32 + lane;  // TMEM lane = token row of this thread
   if (ok) {
+    // dA = scale tril(M1) -> bf16 [i][j] (2 tiles in stage 1)
 #pragma unroll
     for (int cb = 0; cb < 2; ++cb) {
       float r[32];
@@ -726,26 +745,37 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
         *reinterpret_cast<uint4*>(stg + ptx::sw128(i, (cb * 32 + j4 * 8) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-  }
-  // ---- qtil = q e^{G-Gm}, ktil = k e^{Gm-G} in place ----
-  if (ok) ok = ptx::mbar_wait(&bar_qk, 0);
-  if (ok) {
-    // thread: row r = tid & 127, 64 columns of half (tid >> 7)
-    const int r = tid & 127, hf = tid >> 7;
-    unsigned char* qtile = qtl + hf * TILE_BYTES;
-    unsigned char* ktile = ktl + hf * TILE_BYTES;
-    for (int cc = 0; cc < 64; ++cc) {
-      const int col = hf * 64 + cc;
-      const float G = *reinterpret_cast<const float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(r, (col & 31) * 4));
-      const float x = G - Gms[col];
-      st_bf(qtile, r, cc, bf(qtile, r, cc) * __expf(x));
-      st_bf(ktile, r, cc, bf(ktile, r, cc) * __expf(-x));
+    // qtil = q e^{G-Gm}, ktil = k e^{Gm-G}, in place, 8 columns (16 B) per step
+    ok = ptx::mbar_wait(&bar_qk, 0);
+    if (ok) {
+      for (int it = tid; it < 2 * 2 * 128 * 8; it += 256) {
+        const int chunk = it & 7, row = (it >> 3) & 127, tile = it >> 10;  // tile: q0 q1 k0 k1
+        const bool isk = tile >= 2;
+        const int col0 = (tile & 1) * 64 + chunk * 8;
+        unsigned char* t = ring + tile * TILE_BYTES;
+        uint4* pv = reinterpret_cast<uint4*>(t + ptx::sw128(row, chunk * 16));
+        uint4 x = *pv;
+        __nv_bfloat162* x2 = reinterpret_cast<__nv_bfloat162*>(&x);
+        const float4 ga = *reinterpret_cast<const float4*>(Gs + (col0 >> 5) * TILE_BYTES + ptx::sw128(row, (col0 & 31) * 4));
+        const float4 gb = *reinterpret_cast<const float4*>(Gs + (col0 >> 5) * TILE_BYTES +
+                                                            ptx::sw128(row, ((col0 + 4) & 31) * 4));
+        const float G8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __bfloat1622float2(x2[e]);
+          const float d0 = G8[2 * e] - Gms[col0 + 2 * e], d1 = G8[2 * e + 1] - Gms[col0 + 2 * e + 1];
+          f.x *= __expf(isk ? -d0 : d0);
+          f.y *= __expf(isk ? -d1 : d1);
+          x2[e] = __floats2bfloat162_rn(f.x, f.y);
+        }
+        *pv = x;
+      }
     }
   }
   ptx::fence_async_smem();
   ptx::tc_fence_before();
   __syncthreads();
-  if (tid == 0 && ok) {
+  if (tid == 32 && ok) {
     ptx::tc_fence_after();
     const uint32_t ID_KM = ptx::idesc_bf16(128, 128, false, true);
     const uint32_t ID_MM = ptx::idesc_bf16(128, 128, true, true);
@@ -762,7 +792,7 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   }
   if (ok) ok = ptx::mbar_wait(&bar_mma, 1);
   ptx::tc_fence_after();
-  // ---- epilogue: dq, dk (global), dg_raw (in place of G), column sums of e^{GL-G} dki k ----
+  // ---------------- epilogue: dq, dk, dg_raw (in place of G), column sums ----------------
   const int row = row0 + i;
   const bool in = row < p.T;
   const size_t gbase = ((size_t)(b * p.T + (in ? row : 0)) * p.H + h) * p.K + k0;
@@ -774,44 +804,44 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
       ptx::tmem_ld16(tmem_lane_addr(tM5, qd * 32, cb), m5);
       ptx::tmem_ld16(tmem_lane_addr(tM2, qd * 32, cb), m2);
       ptx::tmem_ld16(tmem_lane_addr(tM3, qd * 32, cb), m3);
+      // qtil / ktil of this row, 16 columns: tile cb/64, bytes (cb%64)*2 .. +31
+      const unsigned char* qt_ = qtl + (cb >> 6) * TILE_BYTES;
+      const unsigned char* kt_ = ktl + (cb >> 6) * TILE_BYTES;
+      uint4 qa = *reinterpret_cast<const uint4*>(qt_ + ptx::sw128(i, (cb & 63) * 2));
+      uint4 qb2 = *reinterpret_cast<const uint4*>(qt_ + ptx::sw128(i, (cb & 63) * 2 + 16));
+      uint4 ka = *reinterpret_cast<const uint4*>(kt_ + ptx::sw128(i, (cb & 63) * 2));
+      uint4 kb2 = *reinterpret_cast<const uint4*>(kt_ + ptx::sw128(i, (cb & 63) * 2 + 16));
       ptx::tmem_ld_wait();
       float qv[16], kv[16];
-      if (in) {
-        const uint4* qp = reinterpret_cast<const uint4*>(p.q + gbase + cb);
-        const uint4* kp = reinterpret_cast<const uint4*>(p.k + gbase + cb);
+      {
+        const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&qa);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&qb2);
+        const __nv_bfloat162* d = reinterpret_cast<const __nv_bfloat162*>(&ka);
+        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&kb2);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const uint4 a = qp[u], d = kp[u];
-          const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-          const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 af = __bfloat1622float2(a2[e]), df = __bfloat1622float2(d2[e]);
-            qv[u * 8 + 2 * e] = af.x; qv[u * 8 + 2 * e + 1] = af.y;
-            kv[u * 8 + 2 * e] = df.x; kv[u * 8 + 2 * e + 1] = df.y;
-          }
+        for (int e = 0; e < 4; ++e) {
+          float2 t0 = __bfloat1622float2(a[e]), t1 = __bfloat1622float2(a2[e]);
+          float2 u0 = __bfloat1622float2(d[e]), u1 = __bfloat1622float2(d2[e]);
+          qv[2 * e] = t0.x; qv[2 * e + 1] = t0.y; qv[8 + 2 * e] = t1.x; qv[8 + 2 * e + 1] = t1.y;
+          kv[2 * e] = u0.x; kv[2 * e + 1] = u0.y; kv[8 + 2 * e] = u1.x; kv[8 + 2 * e + 1] = u1.y;
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) qv[e] = kv[e] = 0.f;
       }
       uint32_t dqw[8], dkw[8];
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int col = cb + e;
         float* gp = reinterpret_cast<float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(i, (col & 31) * 4));
-        const float G = *gp;
-        const float x = G - Gms[col];
-        const float dq = __expf(x) * m4[e] + p.scale * __expf(G) * m2[e];
-        const float dki = __expf(GLs[col] - G) * m3[e];
-        const float dk = __expf(-x) * m5[e] + dki;
-        *gp = qv[e] * dq - kv[e] * dk;  // dg_raw
-        float cs = dki * kv[e];
+        const float x = *gp - Gms[col];
+        const float eglm = eGLm[col];
+        const float pq = m4[e] + p.scale * eGm[col] * m2[e];          // dq = e^{x} pq
+        const float pk = m5[e] + eglm * m3[e];                           // dk = e^{-x} pk
+        *gp = in ? qv[e] * pq - kv[e] * pk : 0.f;                       // dg_raw = q dq - k dk
+        float cs = in ? kv[e] * eglm * m3[e] : 0.f;                     // (e^{GL-G} dki) k
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
         if (lane == 0) colsum[qd][col] = cs;
-        m4[e] = dq;
-        m5[e] = dk;
+        m4[e] = __expf(x) * pq;
+        m5[e] = __expf(-x) * pk;
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -830,20 +860,26 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   }
   ptx::tc_fence_before();
   __syncthreads();
-  // ---- dg = reverse cumsum over rows + inter term, one thread per column ----
-  if (ok && tid < 128) {
-    const int col = tid;
-    const float inter = __expf(GLs[col]) * (hdh2[0][col] + hdh2[1][col]) + colsum[0][col] + colsum[1][col] +
-                        colsum[2][col] + colsum[3][col];
-    unsigned char* gt = Gs + (col >> 5) * TILE_BYTES;
-    const uint32_t by = (uint32_t)(col & 31) * 4;
-    float run = 0.f;
-    for (int r = 127; r >= 0; --r) {
+  // ---------------- dg = reverse cumsum over rows + inter term: 2 threads per column ----------------
+  const int col = tid & 127, half = tid >> 7;
+  const unsigned char* gt = Gs + (col >> 5) * TILE_BYTES;
+  const uint32_t by = (uint32_t)(col & 31) * 4;
+  if (ok && half == 1) {
+    float tsum = 0.f;
+    for (int r = 64; r < 128; ++r) tsum += *reinterpret_cast<const float*>(gt + ptx::sw128(r, by));
+    dgtot[col] = tsum;
+  }
+  __syncthreads();
+  if (ok) {
+    const float inter = __expf(GLs[col]) * hdh2[0][col] + colsum[0][col] + colsum[1][col] + colsum[2][col] +
+                        colsum[3][col];
+    float run = half ? 0.f : dgtot[col];
+    for (int r = half * 64 + 63; r >= half * 64; --r) {
       run += *reinterpret_cast<const float*>(gt + ptx::sw128(r, by));
       if (row0 + r < p.T) p.dg[((size_t)(b * p.T + row0 + r) * p.H + h) * p.K + k0 + col] = run + inter;
     }
   }
-  if (!ok && tid == 0) {  // drain loads that may still be in flight
+  if (!ok && tid == 0) {  // drain loads that may still be in flight (bounded)
     ptx::mbar_wait(&full[0], 0);
     ptx::mbar_wait(&full[1], 0);
     ptx::mbar_wait(&bar_qk, 0);
@@ -1016,8 +1052,7 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   }
   {
     LaunchTimer lt(st, "tc_dqk");
-    DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<const bf16*>(q), static_cast<const bf16*>(k),
-                 static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
+    DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
     if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
     k_dqk<<<dim3(s.K / 128, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
     TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
