@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   const bool active = hf < nh;
 
   if (warp == 0) {
-    ptx::tmem_alloc(&tmem_base, 256);
+    ptx::tmem_alloc(&tmem_base, 512);
     ptx::tmem_relinquish();
   }
   if (tid == 0) {
@@ -282,7 +282,10 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tstate = tmem_base;
+  // two TMEM state buffers of 256 columns: the chunk-start state h_c (read) and the
+  // next state D_c h_c + X^T Y (written by the MMA); they swap every chunk, so the
+  // bf16 store of h_c overlaps the MMA that forms h_{c+1}.
+  auto sbuf = [&](int i) { return tmem_base + (uint32_t)((i & 1) * 256); };
   constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, true, true);
 
   auto chunk_of = [&](int i) { return p.reverse ? p.NTb - 1 - i : i; };
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     issue(0);
     if (p.NTb > 1) issue(1);
   }
-  // initial state -> TMEM
+  // initial state -> TMEM buffer 0
   if (active) {
     const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0;
 #pragma unroll
@@ -306,39 +309,43 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
       float r[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[srow + cb * 32 + j] : 0.f;
-      ptx::tmem_st32(tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32), r);
+      ptx::tmem_st32(tmem_lane_addr(sbuf(0), qd * 32, hf * 128 + cb * 32), r);
     }
     ptx::tmem_st_wait();
   }
   bool ok = true;
+  // the decay of chunk i+1 is fetched one iteration ahead (its latency hides behind chunk i)
+  auto decay_of = [&](int i) {
+    return active && i < p.NTb ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
+  };
+  float d_next = decay_of(0);
   for (int i = 0; i < p.NTb; ++i) {
     const int c = chunk_of(i);
+    const float d = d_next;
+    d_next = decay_of(i + 1);
     if (i > 0) {
       ok = ptx::mbar_wait(&bar_mma, (uint32_t)((i - 1) & 1));
       ptx::tc_fence_after();
       if (!ok) break;
       if (tid == 0 && i + 1 < p.NTb) issue(i + 1);  // buffer (i+1)&1 was read by chunk i-1, now complete
     }
-    // TMEM pass: store the chunk-start state (bf16), then scale rows by D_c
+    // pass A: next-state buffer <- D_c * h_c (h_c stays untouched in its buffer)
     if (active) {
-      const float d = p.D[((size_t)(b * p.NTb + c) * p.H + h) * p.K + krow];
-      const size_t srow = ((size_t)((b * p.NTb + c) * p.H + h) * p.K + krow) * p.V + v0;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        float r[32];
-        const uint32_t ta = tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32);
-        ptx::tmem_ld32(ta, r);
+      for (int cb = 0; cb < 4; cb += 2) {
+        float r0[32], r1[32];
+        const uint32_t src = tmem_lane_addr(sbuf(i), qd * 32, hf * 128 + cb * 32);
+        const uint32_t dst = tmem_lane_addr(sbuf(i + 1), qd * 32, hf * 128 + cb * 32);
+        ptx::tmem_ld32(src, r0);
+        ptx::tmem_ld32(src + 32, r1);
         ptx::tmem_ld_wait();
-        if (p.states) {
-          uint4* dst = reinterpret_cast<uint4*>(p.states + srow + cb * 32);
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8)
-            dst[j8] = make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
-                                 ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+        for (int j = 0; j < 32; ++j) {
+          r0[j] *= d;
+          r1[j] *= d;
         }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] *= d;
-        ptx::tmem_st32(ta, r);
+        ptx::tmem_st32(dst, r0);
+        ptx::tmem_st32(dst + 32, r1);
       }
       ptx::tmem_st_wait();
     }
@@ -354,10 +361,30 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
           const unsigned char* xa = buf + (2 * half) * TILE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            ptx::mma_bf16_ss(tstate + half * 128, desc_mnmajor(xa, ks * 2048, TILE_BYTES),
+            ptx::mma_bf16_ss(sbuf(i + 1) + half * 128, desc_mnmajor(xa, ks * 2048, TILE_BYTES),
                              desc_mnmajor(ybuf, ks * 2048, TILE_BYTES), IDESC, 1u);
         }
         ptx::mma_commit(&bar_mma);
+      }
+    }
+    // pass B (overlaps the MMA): store the chunk-start state h_c in bf16
+    if (active && p.states) {
+      const size_t srow = ((size_t)((b * p.NTb + c) * p.H + h) * p.K + krow) * p.V + v0;
+#pragma unroll
+      for (int cb = 0; cb < 4; cb += 2) {
+        float r0[32], r1[32];
+        const uint32_t src = tmem_lane_addr(sbuf(i), qd * 32, hf * 128 + cb * 32);
+        ptx::tmem_ld32(src, r0);
+        ptx::tmem_ld32(src + 32, r1);
+        ptx::tmem_ld_wait();
+        uint4* d0 = reinterpret_cast<uint4*>(p.states + srow + cb * 32);
+#pragma unroll
+        for (int j8 = 0; j8 < 4; ++j8) {
+          d0[j8] = make_uint4(ptx::pack_bf16(r0[j8 * 8 + 0], r0[j8 * 8 + 1]), ptx::pack_bf16(r0[j8 * 8 + 2], r0[j8 * 8 + 3]),
+                              ptx::pack_bf16(r0[j8 * 8 + 4], r0[j8 * 8 + 5]), ptx::pack_bf16(r0[j8 * 8 + 6], r0[j8 * 8 + 7]));
+          d0[4 + j8] = make_uint4(ptx::pack_bf16(r1[j8 * 8 + 0], r1[j8 * 8 + 1]), ptx::pack_bf16(r1[j8 * 8 + 2], r1[j8 * 8 + 3]),
+                                  ptx::pack_bf16(r1[j8 * 8 + 4], r1[j8 * 8 + 5]), ptx::pack_bf16(r1[j8 * 8 + 6], r1[j8 * 8 + 7]));
+        }
       }
     }
     // a failed wait in thread 0 leaves bar_mma pending: the next wait times out for everyone
@@ -369,7 +396,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
-      ptx::tmem_ld32(tmem_lane_addr(tstate, qd * 32, hf * 128 + cb * 32), r);
+      ptx::tmem_ld32(tmem_lane_addr(sbuf(p.NTb), qd * 32, hf * 128 + cb * 32), r);
       ptx::tmem_ld_wait();
       float4* dst = reinterpret_cast<float4*>(p.fin + srow + cb * 32);
 #pragma unroll
@@ -383,7 +410,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 0) ptx::tmem_dealloc(tstate, 256);
+  if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
 }
 
 // ===========================================================================
