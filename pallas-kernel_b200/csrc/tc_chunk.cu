@@ -83,6 +83,19 @@ static bool map_state(CUtensorMap* m, const void* base, int R, int K, int V, int
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// rank-3 store map over per-chunk states with a [32 rows][32 bf16] box and 64-byte swizzle
+static bool map_state_store(CUtensorMap* m, const void* base, int R, int K, int V) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)V, (cuuint64_t)K, (cuuint64_t)R};
+  cuuint64_t strides[2] = {(cuuint64_t)V * 2, (cuuint64_t)K * V * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t es1[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es1,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ---------------------------------------------------------------------------
 // device helpers
 // ---------------------------------------------------------------------------
@@ -251,7 +264,13 @@ struct ScanParams {
 
 struct ScanMaps {
   CUtensorMap x, y;  // x: [B,T,H,K] bf16 box (64,1,128,1); y: [B,T,H,V] bf16 box (64,1,128,1)
+  CUtensorMap st;    // chunk states [B*NTb*H, K, V] bf16, box (32,32,1), 64-byte swizzle (store only)
 };
+
+// byte offset of (row, byte) in a [rows][64 B] tile with 64-byte swizzle (TMA SWIZZLE_64B, 512 B-aligned base)
+__device__ __forceinline__ uint32_t sw64(uint32_t row, uint32_t byte_in_row) {
+  return row * 64u + ((((byte_in_row >> 4) ^ ((row >> 1) & 3u)) << 4) | (byte_in_row & 15u));
+}
 
 __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMaps maps, ScanParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -259,6 +278,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   const int nkb = p.K / 64;              // X tiles per chunk
   const int nh = p.K / 128;              // state halves (TMEM lane blocks)
   const uint32_t buf_bytes = (uint32_t)(nkb + 2) * TILE_BYTES;
+  unsigned char* stage_st = smem + 2 * buf_bytes;  // 8 warps x 2 slots x 2 KB
   __shared__ __align__(8) uint64_t bar_full[2], bar_mma;
   __shared__ uint32_t tmem_base;
 
@@ -367,23 +387,29 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
         ptx::mma_commit(&bar_mma);
       }
     }
-    // pass B (overlaps the MMA): store the chunk-start state h_c in bf16
+    // pass B (overlaps the MMA): store the chunk-start state h_c in bf16.  Each warp stages
+    // 32 rows x 32 columns (2 KB, 64-byte swizzle, conflict-free) and lane 0 issues a TMA
+    // store; two slots per warp alternate so staging overlaps the previous store.
     if (active && p.states) {
-      const size_t srow = ((size_t)((b * p.NTb + c) * p.H + h) * p.K + krow) * p.V + v0;
-#pragma unroll
-      for (int cb = 0; cb < 4; cb += 2) {
-        float r0[32], r1[32];
-        const uint32_t src = tmem_lane_addr(sbuf(i), qd * 32, hf * 128 + cb * 32);
-        ptx::tmem_ld32(src, r0);
-        ptx::tmem_ld32(src + 32, r1);
+      const int rbase = (b * p.NTb + c) * p.H + h;
+#pragma unroll 1
+      for (int cb = 0; cb < 4; ++cb) {
+        float r[32];
+        ptx::tmem_ld32(tmem_lane_addr(sbuf(i), qd * 32, hf * 128 + cb * 32), r);
         ptx::tmem_ld_wait();
-        uint4* d0 = reinterpret_cast<uint4*>(p.states + srow + cb * 32);
+        unsigned char* slot = stage_st + (warp * 2 + (cb & 1)) * 2048;
+        if (lane == 0) ptx::bulk_wait_read<1>();  // the store that last used this slot has read it
+        __syncwarp();
 #pragma unroll
-        for (int j8 = 0; j8 < 4; ++j8) {
-          d0[j8] = make_uint4(ptx::pack_bf16(r0[j8 * 8 + 0], r0[j8 * 8 + 1]), ptx::pack_bf16(r0[j8 * 8 + 2], r0[j8 * 8 + 3]),
-                              ptx::pack_bf16(r0[j8 * 8 + 4], r0[j8 * 8 + 5]), ptx::pack_bf16(r0[j8 * 8 + 6], r0[j8 * 8 + 7]));
-          d0[4 + j8] = make_uint4(ptx::pack_bf16(r1[j8 * 8 + 0], r1[j8 * 8 + 1]), ptx::pack_bf16(r1[j8 * 8 + 2], r1[j8 * 8 + 3]),
-                                  ptx::pack_bf16(r1[j8 * 8 + 4], r1[j8 * 8 + 5]), ptx::pack_bf16(r1[j8 * 8 + 6], r1[j8 * 8 + 7]));
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(slot + sw64(lane, j * 16)) =
+              make_uint4(ptx::pack_bf16(r[j * 8 + 0], r[j * 8 + 1]), ptx::pack_bf16(r[j * 8 + 2], r[j * 8 + 3]),
+                         ptx::pack_bf16(r[j * 8 + 4], r[j * 8 + 5]), ptx::pack_bf16(r[j * 8 + 6], r[j * 8 + 7]));
+        ptx::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::tma_store_3d(&maps.st, v0 + cb * 32, hf * 128 + qd * 32, rbase, slot);
+          ptx::bulk_commit();
         }
       }
     }
@@ -408,6 +434,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     ptx::mbar_wait(&bar_full[0], 0);
     ptx::mbar_wait(&bar_full[1], 0);
   }
+  if (lane == 0) ptx::bulk_wait<0>();  // this warp's state stores are complete
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
@@ -962,7 +989,7 @@ static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
 size_t saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nullptr); }
 
 static size_t prep_smem() { return 6 * TILE_BYTES + 1024; }
-static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 1024; }
+static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 8 * 2 * 2048 + 1024; }
 static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 1024; }
 
 template <typename KernelT>
@@ -986,7 +1013,7 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
              map_tok(&pm.A, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
   ScanMaps sm;
   okm = okm && map_tok(&sm.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+        map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_state_store(&sm.st, sv.h, s.B * NTb * s.H, s.K, s.V);
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
@@ -1047,7 +1074,8 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   ScanMaps sm;
   bool okm = map_tok(&sm.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-             map_tok(&sm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+             map_tok(&sm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+             map_state_store(&sm.st, dhs, s.B * NTb * s.H, s.K, s.V);
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) && map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
