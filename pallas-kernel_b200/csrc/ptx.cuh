@@ -32,6 +32,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// named barrier over `nthreads` threads that also ANDs a predicate across them (so a
+// group of warps takes one decision, e.g. to stop after a bounded wait gave up)
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

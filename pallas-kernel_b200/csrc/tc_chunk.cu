@@ -459,6 +459,7 @@ struct OutMaps {
   CUtensorMap s;   // [B*NTb*H, K, V] box (64,64,1)
   CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1); bwd box (64,1,64,1)
   CUtensorMap y;   // [B,T,H,V] box (64,1,64,1)
+  CUtensorMap o;   // output [B,T,H,V] box (64,1,128,1), store
 };
 
 __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps maps, OutParams p) {
@@ -568,32 +569,41 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
   } else {  // epilogue warps 2..5: lane quadrant (warp & 3)
     const int qd = warp & 3;
     const int i = qd * 32 + lane;
+    unsigned char* stg = smem + OUT_STAGES * STAGE_BYTES;  // [128][128] bf16 as two swizzled [128][64] tiles
+    const bool leader = (warp == 2 && lane == 0);
     uint32_t t = 0;
     for (int it = blockIdx.x; it < items; it += gridDim.x, ++t) {
       int b, c, h, vt;
       decode(it, b, c, h, vt);
       const int ab = t & 1;
-      if (!ptx::mbar_wait(&accf[ab], (t >> 1) & 1)) break;
+      const bool got = ptx::mbar_wait(&accf[ab], (t >> 1) & 1);
+      if (leader) ptx::bulk_wait_read<0>();  // the previous item's store has read the staging tiles
+      if (!ptx::bar_and(1, 128, got)) break;  // all four warps stop together after a timeout
       ptx::tc_fence_after();
-      const int row = c * BT + i;
-      bf16* dst = p.out + ((size_t)(b * p.T + row) * p.H + h) * p.V + vt * BV;
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         float r[32];
         ptx::tmem_ld32(tmem_lane_addr(tacc, qd * 32, ab * 128 + cb * 32), r);
         ptx::tmem_ld_wait();
-        if (row < p.T) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + cb * 32);
+        unsigned char* tile = stg + (cb >> 1) * TILE_BYTES;
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8)
-            d4[j8] = make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
-                                ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
-        }
+        for (int j8 = 0; j8 < 4; ++j8)
+          *reinterpret_cast<uint4*>(tile + ptx::sw128(i, (cb & 1) * 64 + j8 * 16)) =
+              make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
+                         ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&acce[ab]);
+      if (lane == 0) ptx::mbar_arrive(&acce[ab]);  // TMEM accumulator free for the next item
+      ptx::fence_async_smem();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (leader) {  // rows past T are clipped by the tensor map
+        ptx::tma_store_4d(&maps.o, vt * BV, h, c * BT, b, stg);
+        ptx::tma_store_4d(&maps.o, vt * BV + 64, h, c * BT, b, stg + TILE_BYTES);
+        ptx::bulk_commit();
+      }
     }
+    if (leader) ptx::bulk_wait<0>();
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -626,6 +636,7 @@ struct DqkMaps {
   CUtensorMap hs, dhs; // [B*NTb*H, K, V] box (64,128,1)
   CUtensorMap g;       // [B,T,H,K] fp32 box (32,1,128,1)
   CUtensorMap q, k;    // [B,T,H,K] bf16 box (64,1,128,1)
+  CUtensorMap dq, dk;  // [B,T,H,K] bf16 box (64,1,128,1), stores
 };
 
 __device__ __forceinline__ float gval(const unsigned char* Gs, int row, int col) {
@@ -640,7 +651,8 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   unsigned char* Gs = smem + 2 * STG;       // 4 x [128][32] fp32: G, then dg_raw
   unsigned char* qtl = ring;                // after the stream: qtil (2 tiles), ktil (2 tiles)
   unsigned char* ktl = ring + 2 * TILE_BYTES;
-  unsigned char* dAs = ring + STG;          // dA bf16 (2 tiles)
+  unsigned char* dAs = ring + STG;          // dA bf16 (2 tiles), later the dk staging tiles
+  unsigned char* dqs = ring + STG + 2 * TILE_BYTES;  // dq staging tiles (free after the V stream)
   __shared__ float GLs[128], Gms[128], eGm[128], eGLm[128], hdh2[2][128], colsum[4][128], dgtot[128];
   __shared__ __align__(8) uint64_t full[2], empty[2], bar_g, bar_qk, bar_mma;
   __shared__ uint32_t tmem_base;
@@ -849,7 +861,6 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   // ---------------- epilogue: dq, dk, dg_raw (in place of G), column sums ----------------
   const int row = row0 + i;
   const bool in = row < p.T;
-  const size_t gbase = ((size_t)(b * p.T + (in ? row : 0)) * p.H + h) * p.K + k0;
   if (ok) {
     for (int g16 = 0; g16 < 4; ++g16) {
       const int cb = ch * 64 + g16 * 16;  // first column of this group
@@ -902,18 +913,26 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
         dqw[u] = ptx::pack_bf16(m4[2 * u], m4[2 * u + 1]);
         dkw[u] = ptx::pack_bf16(m5[2 * u], m5[2 * u + 1]);
       }
-      if (in) {
-        uint4* dqp = reinterpret_cast<uint4*>(p.dq + gbase + cb);
-        uint4* dkp = reinterpret_cast<uint4*>(p.dk + gbase + cb);
-        dqp[0] = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
-        dqp[1] = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
-        dkp[0] = make_uint4(dkw[0], dkw[1], dkw[2], dkw[3]);
-        dkp[1] = make_uint4(dkw[4], dkw[5], dkw[6], dkw[7]);
-      }
+      // stage [128 rows][128 cols] bf16 as two 128B-swizzled [128][64] tiles each
+      unsigned char* tq = dqs + (cb >> 6) * TILE_BYTES;
+      unsigned char* tk = dAs + (cb >> 6) * TILE_BYTES;
+      const uint32_t by = (uint32_t)(cb & 63) * 2;
+      *reinterpret_cast<uint4*>(tq + ptx::sw128(i, by)) = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
+      *reinterpret_cast<uint4*>(tq + ptx::sw128(i, by + 16)) = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
+      *reinterpret_cast<uint4*>(tk + ptx::sw128(i, by)) = make_uint4(dkw[0], dkw[1], dkw[2], dkw[3]);
+      *reinterpret_cast<uint4*>(tk + ptx::sw128(i, by + 16)) = make_uint4(dkw[4], dkw[5], dkw[6], dkw[7]);
     }
   }
+  ptx::fence_async_smem();
   ptx::tc_fence_before();
   __syncthreads();
+  if (tid == 0 && ok) {  // dq, dk tiles -> global (rows past T are clipped by the tensor map)
+    ptx::tma_store_4d(&maps.dq, k0, h, row0, b, dqs);
+    ptx::tma_store_4d(&maps.dq, k0 + 64, h, row0, b, dqs + TILE_BYTES);
+    ptx::tma_store_4d(&maps.dk, k0, h, row0, b, dAs);
+    ptx::tma_store_4d(&maps.dk, k0 + 64, h, row0, b, dAs + TILE_BYTES);
+    ptx::bulk_commit();
+  }
   // ---------------- dg = reverse cumsum over rows + inter term: 2 threads per column ----------------
   const int col = tid & 127, half = tid >> 7;
   const unsigned char* gt = Gs + (col >> 5) * TILE_BYTES;
@@ -938,6 +957,7 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
     ptx::mbar_wait(&full[1], 0);
     ptx::mbar_wait(&bar_qk, 0);
   }
+  if (tid == 0) ptx::bulk_wait<0>();
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
@@ -990,7 +1010,7 @@ size_t saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nul
 
 static size_t prep_smem() { return 6 * TILE_BYTES + 1024; }
 static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 8 * 2 * 2048 + 1024; }
-static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 1024; }
+static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 2 * TILE_BYTES + 1024; }
 
 template <typename KernelT>
 static cudaError_t set_smem(KernelT k, size_t bytes) {
@@ -1017,7 +1037,8 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
-        map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) && map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64);
+        map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) && map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64) &&
+        map_tok(&om.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   {
@@ -1079,14 +1100,15 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) && map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
-        map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64);
+        map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   DqkMaps dm;
   okm = okm && map_tok(&dm.dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
         map_tok(&dm.v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
         map_state(&dm.hs, sv.h, s.B * NTb * s.H, s.K, s.V, 128) &&
         map_state(&dm.dhs, dhs, s.B * NTb * s.H, s.K, s.V, 128) &&
         map_tok(&dm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_tok(&dm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
+        map_tok(&dm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm.dq, dq, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   {
