@@ -611,7 +611,9 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 }
 
 // ===========================================================================
-// k_dqk: dq, dk, dg of one (batch, chunk, head, 128-wide K tile).  grid (K/128, NTb, B*H), 256 threads.
+// k_dqk: dq, dk, dg of one (batch, chunk, head, 64-wide K tile).  grid (K/64, NTb, B*H),
+// 256 threads, two CTAs per SM (256 TMEM columns and ~100 KB shared memory each), so one
+// CTA's epilogue runs while the other streams its operands.
 //   dA      = scale tril(do v^T)                            (M1, contraction over V)
 //   dqi     = do h_c^T            dki = v dh_c^T            (M2, M3, contraction over V)
 //   dq      = e^{G-Gm} (dA ktil + scale e^{Gm} dqi)         (M4 = dA x ktil,  ktil = k e^{Gm-G})
@@ -620,10 +622,12 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 //             with q dq = qtil (M4 + scale e^{Gm} dqi) and k dk = ktil (M5 + e^{GL-Gm} dki)
 // (reference chunk_gla_bwd_fused_kernel tops/ops/gla/chunk.py:1423-1479 and the
 //  _ref functions :504-743).
-// Roles during the V stream: warp 0 = TMA producer, warp 1 = MMA issuer, warps 2-3 =
-// chunk-local cumsum of g (in place), warps 4-7 = sum_v h*dh.  The 2-stage operand
-// ring is released by the MMA commit plus the four reducer warps.  After the stream
-// the ring holds q -> qtil, k -> ktil (stage 0) and the bf16 dA (stage 1).
+// During the V stream warp 0 is the TMA producer, warp 1 the MMA issuer and warps 4-7
+// sum h*dh over V; the 2-stage ring is released by the MMA commit plus those four warps.
+// After the stream stage 0 holds g -> G -> dg (fp32, in place) and q -> qtil -> dq,
+// stage 1 holds k -> ktil -> dk and the bf16 dA; the outputs leave by TMA stores.
+// dA is the same for every K tile of a chunk; the do/v re-reads of the K tiles of one
+// chunk (adjacent CTAs) are served by L2.
 // ===========================================================================
 struct DqkParams {
   int B, T, H, K, V, NTb;
@@ -632,146 +636,151 @@ struct DqkParams {
 };
 
 struct DqkMaps {
-  CUtensorMap dO, v;   // [B,T,H,V] box (64,1,128,1)
-  CUtensorMap hs, dhs; // [B*NTb*H, K, V] box (64,128,1)
-  CUtensorMap g;       // [B,T,H,K] fp32 box (32,1,128,1)
+  CUtensorMap dO, v;   // [B,T,H,V] bf16 box (64,1,128,1)
+  CUtensorMap hs, dhs; // [B*NTb*H, K, V] bf16 box (64,64,1)
+  CUtensorMap g, dg;   // [B,T,H,K] fp32 box (32,1,128,1); dg is a store map
   CUtensorMap q, k;    // [B,T,H,K] bf16 box (64,1,128,1)
   CUtensorMap dq, dk;  // [B,T,H,K] bf16 box (64,1,128,1), stores
 };
 
-__device__ __forceinline__ float gval(const unsigned char* Gs, int row, int col) {
-  return *reinterpret_cast<const float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(row, (col & 31) * 4));
+constexpr uint32_t DQK_STG = 3 * TILE_BYTES;  // do 16K, v 16K, h 8K, dh 8K
+
+// Sum of 16 per-lane values over the 32 lanes of a warp, for 16 columns at once: a
+// transposing butterfly (each step keeps half the columns and adds the partner's
+// other half).  Returns the full sum of column dqk_red_col(lane) (valid in every lane).
+__device__ __forceinline__ int dqk_red_col(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+__device__ __forceinline__ float dqk_reduce16(const float (&v)[16], int lane) {
+  float r8[8], r4[4], r2[2];
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float keep = u16 ? v[j + 8] : v[j], send = u16 ? v[j] : v[j + 8];
+    r8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float keep = u8 ? r8[j + 4] : r8[j], send = u8 ? r8[j] : r8[j + 4];
+    r4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float keep = u4 ? r4[j + 2] : r4[j], send = u4 ? r4[j] : r4[j + 2];
+    r2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  const float keep = u2 ? r2[1] : r2[0], send = u2 ? r2[0] : r2[1];
+  const float r1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  return r1 + __shfl_xor_sync(0xffffffffu, r1, 1);
 }
 
-__global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps maps, DqkParams p) {
+__global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps maps, DqkParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr uint32_t STG = 4 * TILE_BYTES;  // do, v, h, dh tiles of one V block
-  unsigned char* ring = smem;               // 2 stages
-  unsigned char* Gs = smem + 2 * STG;       // 4 x [128][32] fp32: G, then dg_raw
-  unsigned char* qtl = ring;                // after the stream: qtil (2 tiles), ktil (2 tiles)
-  unsigned char* ktl = ring + 2 * TILE_BYTES;
-  unsigned char* dAs = ring + STG;          // dA bf16 (2 tiles), later the dk staging tiles
-  unsigned char* dqs = ring + STG + 2 * TILE_BYTES;  // dq staging tiles (free after the V stream)
-  __shared__ float GLs[128], Gms[128], eGm[128], eGLm[128], hdh2[2][128], colsum[4][128], dgtot[128];
-  __shared__ __align__(8) uint64_t full[2], empty[2], bar_g, bar_qk, bar_mma;
+  unsigned char* Gs = smem;                           // two fp32 [128][32] tiles: g -> G -> dg
+  unsigned char* qtl = smem + 2 * TILE_BYTES;         // q -> qtil -> dq staging
+  unsigned char* ktl = smem + DQK_STG;                // k -> ktil -> dk staging
+  unsigned char* dAs = smem + DQK_STG + TILE_BYTES;   // dA bf16 [128][128] as two [128][64] tiles
+  __shared__ __align__(16) float cS[64], cL[64], cGL[64];  // scale e^{Gm}, e^{GL-Gm}, e^{GL} per column
+  __shared__ float hdh2[2][64], colsum[4][64], segs[4][64];
+  __shared__ __align__(8) uint64_t full[2], empty[2], bar_g, bar_q, bar_k, bar_mma;
   __shared__ uint32_t tmem_base;
 
   const int kt = blockIdx.x, c = blockIdx.y, b = blockIdx.z / p.H, h = blockIdx.z % p.H;
-  const int k0 = kt * 128, row0 = c * BT;
+  const int k0 = kt * 64, row0 = c * BT;
   const int srow = (b * p.NTb + c) * p.H + h;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nvb = p.V / 64;
+  const int nvb = p.V / 64;  // even: V is a multiple of 128
 
   if (warp == 0) {
-    ptx::tmem_alloc(&tmem_base, 512);
+    ptx::tmem_alloc(&tmem_base, 256);
     ptx::tmem_relinquish();
   }
   if (tid == 32) {
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 reducer warps
+    for (int s_ = 0; s_ < 2; ++s_) {
+      ptx::mbar_init(&full[s_], 1);
+      ptx::mbar_init(&empty[s_], 1 + 4);  // MMA commit + 4 reducer warps
     }
     ptx::mbar_init(&bar_g, 1);
-    ptx::mbar_init(&bar_qk, 1);
+    ptx::mbar_init(&bar_q, 1);
+    ptx::mbar_init(&bar_k, 1);
     ptx::mbar_init(&bar_mma, 1);
     ptx::fence_mbar_init();
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tM1 = tmem_base, tM2 = tmem_base + 128, tM3 = tmem_base + 256, tM5 = tmem_base + 384;
+  const uint32_t tM1 = tmem_base, tM2 = tmem_base + 128, tM3 = tmem_base + 192;
   bool ok = true;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(&bar_g, 4 * TILE_BYTES);
-      for (int j = 0; j < 4; ++j) ptx::tma_load_4d(Gs + j * TILE_BYTES, &maps.g, k0 + 32 * j, h, row0, b, &bar_g);
       for (int vb = 0; vb < nvb && ok; ++vb) {
-        const int s = vb & 1;
-        if (vb >= 2) ok = ptx::mbar_wait(&empty[s], (uint32_t)(((vb >> 1) - 1) & 1));
+        const int st = vb & 1;
+        if (vb >= 2) ok = ptx::mbar_wait(&empty[st], (uint32_t)(((vb >> 1) - 1) & 1));
         if (!ok) break;
-        unsigned char* st = ring + s * STG;
-        ptx::mbar_arrive_expect_tx(&full[s], STG);
-        ptx::tma_load_4d(st, &maps.dO, vb * 64, h, row0, b, &full[s]);
-        ptx::tma_load_4d(st + TILE_BYTES, &maps.v, vb * 64, h, row0, b, &full[s]);
-        ptx::tma_load_3d(st + 2 * TILE_BYTES, &maps.hs, vb * 64, k0, srow, &full[s]);
-        ptx::tma_load_3d(st + 3 * TILE_BYTES, &maps.dhs, vb * 64, k0, srow, &full[s]);
+        unsigned char* sp = smem + st * DQK_STG;
+        ptx::mbar_arrive_expect_tx(&full[st], DQK_STG);
+        ptx::tma_load_4d(sp, &maps.dO, vb * 64, h, row0, b, &full[st]);
+        ptx::tma_load_4d(sp + TILE_BYTES, &maps.v, vb * 64, h, row0, b, &full[st]);
+        ptx::tma_load_3d(sp + 2 * TILE_BYTES, &maps.hs, vb * 64, k0, srow, &full[st]);
+        ptx::tma_load_3d(sp + 2 * TILE_BYTES + TILE_BYTES / 2, &maps.dhs, vb * 64, k0, srow, &full[st]);
       }
-      // stage 0 gets q and k once its last V block is released
+      // stage 0 is last used by V block nvb-2, stage 1 by nvb-1
+      if (ok) ok = ptx::mbar_wait(&empty[0], (uint32_t)(((nvb - 2) >> 1) & 1));
       if (ok) {
-        const int last0 = (nvb - 1) & ~1;  // last V block that used stage 0
-        ok = ptx::mbar_wait(&empty[0], (uint32_t)((last0 >> 1) & 1));
+        ptx::mbar_arrive_expect_tx(&bar_g, 2 * TILE_BYTES);
+        ptx::tma_load_4d(Gs, &maps.g, k0, h, row0, b, &bar_g);
+        ptx::tma_load_4d(Gs + TILE_BYTES, &maps.g, k0 + 32, h, row0, b, &bar_g);
+        ptx::mbar_arrive_expect_tx(&bar_q, TILE_BYTES);
+        ptx::tma_load_4d(qtl, &maps.q, k0, h, row0, b, &bar_q);
       }
+      if (ok) ok = ptx::mbar_wait(&empty[1], (uint32_t)(((nvb - 1) >> 1) & 1));
       if (ok) {
-        ptx::mbar_arrive_expect_tx(&bar_qk, 4 * TILE_BYTES);
-        ptx::tma_load_4d(qtl, &maps.q, k0, h, row0, b, &bar_qk);
-        ptx::tma_load_4d(qtl + TILE_BYTES, &maps.q, k0 + 64, h, row0, b, &bar_qk);
-        ptx::tma_load_4d(ktl, &maps.k, k0, h, row0, b, &bar_qk);
-        ptx::tma_load_4d(ktl + TILE_BYTES, &maps.k, k0 + 64, h, row0, b, &bar_qk);
+        ptx::mbar_arrive_expect_tx(&bar_k, TILE_BYTES);
+        ptx::tma_load_4d(ktl, &maps.k, k0, h, row0, b, &bar_k);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer for the V stream ----------------
     if (lane == 0) {
-      constexpr uint32_t ID_KK = ptx::idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_N128 = ptx::idesc_bf16(128, 128, false, false);
+      constexpr uint32_t ID_N64 = ptx::idesc_bf16(128, 64, false, false);
       for (int vb = 0; vb < nvb && ok; ++vb) {
-        const int s = vb & 1;
-        ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
+        const int st = vb & 1;
+        ok = ptx::mbar_wait(&full[st], (uint32_t)((vb >> 1) & 1));
         if (!ok) break;
         ptx::tc_fence_after();
-        const unsigned char* st = ring + s * STG;
+        const unsigned char* sp = smem + st * DQK_STG;
+        const unsigned char* th = sp + 2 * TILE_BYTES;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint32_t acc = (vb | ks) ? 1u : 0u;
-          ptx::mma_bf16_ss(tM1, desc_kmajor(st, ks * 32), desc_kmajor(st + TILE_BYTES, ks * 32), ID_KK, acc);
-          ptx::mma_bf16_ss(tM2, desc_kmajor(st, ks * 32), desc_kmajor(st + 2 * TILE_BYTES, ks * 32), ID_KK, acc);
-          ptx::mma_bf16_ss(tM3, desc_kmajor(st + TILE_BYTES, ks * 32), desc_kmajor(st + 3 * TILE_BYTES, ks * 32),
-                           ID_KK, acc);
+          ptx::mma_bf16_ss(tM1, desc_kmajor(sp, ks * 32), desc_kmajor(sp + TILE_BYTES, ks * 32), ID_N128, acc);
+          ptx::mma_bf16_ss(tM2, desc_kmajor(sp, ks * 32), desc_kmajor(th, ks * 32), ID_N64, acc);
+          ptx::mma_bf16_ss(tM3, desc_kmajor(sp + TILE_BYTES, ks * 32), desc_kmajor(th + TILE_BYTES / 2, ks * 32),
+                           ID_N64, acc);
         }
-        ptx::mma_commit(&empty[s]);
+        ptx::mma_commit(&empty[st]);
       }
       if (ok) ptx::mma_commit(&bar_mma);
     }
-  } else if (warp < 4) {
-    // ---------------- chunk-local cumsum of g, in place (2 columns per thread) ----------------
-    ok = ptx::mbar_wait(&bar_g, 0);
-    if (ok) {
-      const int c0 = (tid - 64) * 2;
-      float r0 = 0.f, r1 = 0.f;
-      for (int r = 0; r < 128; ++r) {
-        float* e0 = reinterpret_cast<float*>(Gs + (c0 >> 5) * TILE_BYTES + ptx::sw128(r, (c0 & 31) * 4));
-        const float2 x = *reinterpret_cast<float2*>(e0);
-        r0 += x.x;
-        r1 += x.y;
-        *reinterpret_cast<float2*>(e0) = make_float2(r0, r1);
-        if (r == 63) {
-          Gms[c0] = r0;
-          Gms[c0 + 1] = r1;
-        }
-      }
-      GLs[c0] = r0;
-      GLs[c0 + 1] = r1;
-      eGm[c0] = __expf(Gms[c0]);
-      eGm[c0 + 1] = __expf(Gms[c0 + 1]);
-      eGLm[c0] = __expf(r0 - Gms[c0]);
-      eGLm[c0 + 1] = __expf(r1 - Gms[c0 + 1]);
-    }
-  } else {
-    // ---------------- sum_v h*dh of the state rows, per V block ----------------
-    const int hr = (tid - 128);  // state row 0..127
+  } else if (warp >= 4) {
+    // ---------------- sum_v h*dh of the 64 state rows: 2 threads per row ----------------
+    const int hr = (tid - 128) & 63, hv = (tid - 128) >> 6;
     float acc = 0.f;
     for (int vb = 0; vb < nvb && ok; ++vb) {
-      const int s = vb & 1;
-      ok = ptx::mbar_wait(&full[s], (uint32_t)((vb >> 1) & 1));
+      const int st = vb & 1;
+      ok = ptx::mbar_wait(&full[st], (uint32_t)((vb >> 1) & 1));
       if (!ok) break;
-      const unsigned char* th = ring + s * STG + 2 * TILE_BYTES;
-      const unsigned char* tdh = th + TILE_BYTES;
+      const unsigned char* th = smem + st * DQK_STG + 2 * TILE_BYTES;
+      const unsigned char* tdh = th + TILE_BYTES / 2;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 a = *reinterpret_cast<const uint4*>(th + ptx::sw128(hr, u * 16));
-        const uint4 d = *reinterpret_cast<const uint4*>(tdh + ptx::sw128(hr, u * 16));
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t off = ptx::sw128(hr, (hv * 4 + u) * 16);
+        const uint4 a = *reinterpret_cast<const uint4*>(th + off);
+        const uint4 d = *reinterpret_cast<const uint4*>(tdh + off);
         const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
         const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
 #pragma unroll
@@ -781,18 +790,19 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
         }
       }
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&empty[s]);
+      if (lane == 0) ptx::mbar_arrive(&empty[st]);
     }
-    hdh2[0][hr] = acc;
+    hdh2[hv][hr] = acc;
   }
-  // ---------------- all threads: V-stream MMAs done, G done ----------------
+
+  // ---------------- all threads: dA from M1 once the V-stream MMAs are done ----------------
   __syncthreads();
   if (ok) ok = ptx::mbar_wait(&bar_mma, 0);
   ptx::tc_fence_after();
   const int qd = warp & 3, ch = warp >> 2;
   const int i = qd * 32 + lane;  // TMEM lane = token row of this thread
   if (ok) {
-    // dA = scale tril(M1) -> bf16 [i][j] (2 tiles in stage 1)
+    // dA = scale tril(M1) -> bf16 [i][j]; this warp writes columns ch*64.. (tile ch)
 #pragma unroll
     for (int cb = 0; cb < 2; ++cb) {
       float r[32];
@@ -811,31 +821,64 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
         *reinterpret_cast<uint4*>(stg + ptx::sw128(i, (cb * 32 + j4 * 8) * 2)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
-    // qtil = q e^{G-Gm}, ktil = k e^{Gm-G}, in place, 8 columns (16 B) per step
-    ok = ptx::mbar_wait(&bar_qk, 0);
-    if (ok) {
-      for (int it = tid; it < 2 * 2 * 128 * 8; it += 256) {
-        const int chunk = it & 7, row = (it >> 3) & 127, tile = it >> 10;  // tile: q0 q1 k0 k1
-        const bool isk = tile >= 2;
-        const int col0 = (tile & 1) * 64 + chunk * 8;
-        unsigned char* t = ring + tile * TILE_BYTES;
-        uint4* pv = reinterpret_cast<uint4*>(t + ptx::sw128(row, chunk * 16));
-        uint4 x = *pv;
-        __nv_bfloat162* x2 = reinterpret_cast<__nv_bfloat162*>(&x);
-        const float4 ga = *reinterpret_cast<const float4*>(Gs + (col0 >> 5) * TILE_BYTES + ptx::sw128(row, (col0 & 31) * 4));
-        const float4 gb = *reinterpret_cast<const float4*>(Gs + (col0 >> 5) * TILE_BYTES +
-                                                            ptx::sw128(row, ((col0 + 4) & 31) * 4));
-        const float G8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+  }
+  // ---------------- chunk-local cumsum of g: thread (column, 32-row segment) ----------------
+  // The tile is overwritten with x = G - Gm (Gm = G at row 63, the mid-chunk reference).
+  const int gcol = tid & 63, seg = tid >> 6;
+  unsigned char* gt = Gs + (gcol >> 5) * TILE_BYTES;
+  const uint32_t gby = (uint32_t)(gcol & 31) * 4;
+  float gv[32];
+  if (ok) ok = ptx::mbar_wait(&bar_g, 0);
+  if (ok) {
+    float sum = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float2 f = __bfloat1622float2(x2[e]);
-          const float d0 = G8[2 * e] - Gms[col0 + 2 * e], d1 = G8[2 * e + 1] - Gms[col0 + 2 * e + 1];
-          f.x *= __expf(isk ? -d0 : d0);
-          f.y *= __expf(isk ? -d1 : d1);
-          x2[e] = __floats2bfloat162_rn(f.x, f.y);
-        }
-        *pv = x;
+    for (int r = 0; r < 32; ++r) {
+      gv[r] = *reinterpret_cast<const float*>(gt + ptx::sw128(seg * 32 + r, gby));
+      sum += gv[r];
+    }
+    segs[seg][gcol] = sum;
+  }
+  __syncthreads();
+  if (ok) {
+    const float gm = segs[0][gcol] + segs[1][gcol];
+    float run = -gm;
+    for (int s2 = 0; s2 < seg; ++s2) run += segs[s2][gcol];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      run += gv[r];
+      *reinterpret_cast<float*>(gt + ptx::sw128(seg * 32 + r, gby)) = run;
+    }
+    if (seg == 0) {
+      const float glm = segs[2][gcol] + segs[3][gcol];  // GL - Gm
+      cS[gcol] = p.scale * __expf(gm);
+      cL[gcol] = __expf(glm);
+      cGL[gcol] = __expf(gm + glm);
+    }
+  }
+  __syncthreads();
+  // ---------------- qtil = q e^{G-Gm}, ktil = k e^{Gm-G}, in place, 8 columns per item ----------------
+  if (ok) ok = ptx::mbar_wait(&bar_q, 0);
+  if (ok) ok = ptx::mbar_wait(&bar_k, 0);
+  if (ok) {
+    for (int it = tid; it < 128 * 8; it += 256) {
+      const int chunk = it & 7, row = it >> 3, col0 = chunk * 8;
+      const unsigned char* gp = Gs + (col0 >> 5) * TILE_BYTES;
+      const float4 ga = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, (col0 & 31) * 4));
+      const float4 gb = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, (col0 & 31) * 4 + 16));
+      const float x8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      uint4* pq = reinterpret_cast<uint4*>(qtl + ptx::sw128(row, chunk * 16));
+      uint4* pk = reinterpret_cast<uint4*>(ktl + ptx::sw128(row, chunk * 16));
+      uint4 xq = *pq, xk = *pk;
+      __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&xq);
+      __nv_bfloat162* k2 = reinterpret_cast<__nv_bfloat162*>(&xk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = __bfloat1622float2(q2[e]), fk = __bfloat1622float2(k2[e]);
+        q2[e] = __floats2bfloat162_rn(fq.x * __expf(x8[2 * e]), fq.y * __expf(x8[2 * e + 1]));
+        k2[e] = __floats2bfloat162_rn(fk.x * __expf(-x8[2 * e]), fk.y * __expf(-x8[2 * e + 1]));
       }
+      *pq = xq;
+      *pk = xk;
     }
   }
   ptx::fence_async_smem();
@@ -843,124 +886,142 @@ __global__ void __launch_bounds__(256, 1) k_dqk(const __grid_constant__ DqkMaps 
   __syncthreads();
   if (tid == 32 && ok) {
     ptx::tc_fence_after();
-    const uint32_t ID_KM = ptx::idesc_bf16(128, 128, false, true);
-    const uint32_t ID_MM = ptx::idesc_bf16(128, 128, true, true);
+    constexpr uint32_t ID_KM = ptx::idesc_bf16(128, 64, false, true);
+    constexpr uint32_t ID_MM = ptx::idesc_bf16(128, 64, true, true);
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      // M4 (into M1's columns): dA[i][j] x ktil[j][k]
+      // M4 (M1 columns 0..63): dA[i][j] x ktil[j][k]
       ptx::mma_bf16_ss(tM1, desc_kmajor(dAs + (ks >> 2) * TILE_BYTES, (ks & 3) * 32),
                        desc_mnmajor(ktl, ks * 2048, TILE_BYTES), ID_KM, ks ? 1u : 0u);
-      // M5: dA^T[j][i] x qtil[i][k]
-      ptx::mma_bf16_ss(tM5, desc_mnmajor(dAs, ks * 2048, TILE_BYTES), desc_mnmajor(qtl, ks * 2048, TILE_BYTES),
+      // M5 (M1 columns 64..127): dA^T[j][i] x qtil[i][k]
+      ptx::mma_bf16_ss(tM1 + 64, desc_mnmajor(dAs, ks * 2048, TILE_BYTES), desc_mnmajor(qtl, ks * 2048, TILE_BYTES),
                        ID_MM, ks ? 1u : 0u);
     }
     ptx::mma_commit(&bar_mma);
   }
   if (ok) ok = ptx::mbar_wait(&bar_mma, 1);
   ptx::tc_fence_after();
-  // ---------------- epilogue: dq, dk, dg_raw (in place of G), column sums ----------------
-  const int row = row0 + i;
-  const bool in = row < p.T;
+  // ---------------- epilogue: dq, dk (in place of qtil, ktil), dg_raw (in place of x), column sums ----------------
+  // Rows past T need no mask: their q, k, v, do were zero-filled by the loads, so every
+  // term below is zero there, and the stores clip them.
   if (ok) {
-    for (int g16 = 0; g16 < 4; ++g16) {
-      const int cb = ch * 64 + g16 * 16;  // first column of this group
+#pragma unroll 1
+    for (int g16 = 0; g16 < 2; ++g16) {
+      const int cb = ch * 32 + g16 * 16;  // first column of this group
       float m4[16], m5[16], m2[16], m3[16];
       ptx::tmem_ld16(tmem_lane_addr(tM1, qd * 32, cb), m4);
-      ptx::tmem_ld16(tmem_lane_addr(tM5, qd * 32, cb), m5);
+      ptx::tmem_ld16(tmem_lane_addr(tM1 + 64, qd * 32, cb), m5);
       ptx::tmem_ld16(tmem_lane_addr(tM2, qd * 32, cb), m2);
       ptx::tmem_ld16(tmem_lane_addr(tM3, qd * 32, cb), m3);
-      // qtil / ktil of this row, 16 columns: tile cb/64, bytes (cb%64)*2 .. +31
-      const unsigned char* qt_ = qtl + (cb >> 6) * TILE_BYTES;
-      const unsigned char* kt_ = ktl + (cb >> 6) * TILE_BYTES;
-      uint4 qa = *reinterpret_cast<const uint4*>(qt_ + ptx::sw128(i, (cb & 63) * 2));
-      uint4 qb2 = *reinterpret_cast<const uint4*>(qt_ + ptx::sw128(i, (cb & 63) * 2 + 16));
-      uint4 ka = *reinterpret_cast<const uint4*>(kt_ + ptx::sw128(i, (cb & 63) * 2));
-      uint4 kb2 = *reinterpret_cast<const uint4*>(kt_ + ptx::sw128(i, (cb & 63) * 2 + 16));
-      ptx::tmem_ld_wait();
+      const uint32_t qb = ptx::sw128(i, cb * 2), qb2 = ptx::sw128(i, cb * 2 + 16);
+      const uint4 qa = *reinterpret_cast<const uint4*>(qtl + qb), qa2 = *reinterpret_cast<const uint4*>(qtl + qb2);
+      const uint4 ka = *reinterpret_cast<const uint4*>(ktl + qb), ka2 = *reinterpret_cast<const uint4*>(ktl + qb2);
+      unsigned char* gp = Gs + (cb >> 5) * TILE_BYTES;
+      float gv[16];  // x = G - Gm of this row
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 t4 = *reinterpret_cast<const float4*>(gp + ptx::sw128(i, (cb & 31) * 4 + u * 16));
+        gv[4 * u] = t4.x; gv[4 * u + 1] = t4.y; gv[4 * u + 2] = t4.z; gv[4 * u + 3] = t4.w;
+      }
       float qv[16], kv[16];
       {
         const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&qa);
-        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&qb2);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&qa2);
         const __nv_bfloat162* d = reinterpret_cast<const __nv_bfloat162*>(&ka);
-        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&kb2);
+        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&ka2);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float2 t0 = __bfloat1622float2(a[e]), t1 = __bfloat1622float2(a2[e]);
-          float2 u0 = __bfloat1622float2(d[e]), u1 = __bfloat1622float2(d2[e]);
+          const float2 t0 = __bfloat1622float2(a[e]), t1 = __bfloat1622float2(a2[e]);
+          const float2 u0 = __bfloat1622float2(d[e]), u1 = __bfloat1622float2(d2[e]);
           qv[2 * e] = t0.x; qv[2 * e + 1] = t0.y; qv[8 + 2 * e] = t1.x; qv[8 + 2 * e + 1] = t1.y;
           kv[2 * e] = u0.x; kv[2 * e + 1] = u0.y; kv[8 + 2 * e] = u1.x; kv[8 + 2 * e + 1] = u1.y;
         }
       }
-      uint32_t dqw[8], dkw[8];
+      ptx::tmem_ld_wait();
+      float cs[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int col = cb + e;
-        float* gp = reinterpret_cast<float*>(Gs + (col >> 5) * TILE_BYTES + ptx::sw128(i, (col & 31) * 4));
-        const float x = *gp - Gms[col];
-        const float eglm = eGLm[col];
-        const float pq = m4[e] + p.scale * eGm[col] * m2[e];          // dq = e^{x} pq
-        const float pk = m5[e] + eglm * m3[e];                           // dk = e^{-x} pk
-        *gp = in ? qv[e] * pq - kv[e] * pk : 0.f;                       // dg_raw = q dq - k dk
-        float cs = in ? kv[e] * eglm * m3[e] : 0.f;                     // (e^{GL-G} dki) k
+      for (int u = 0; u < 4; ++u) {
+        const float4 f4s = *reinterpret_cast<const float4*>(&cS[cb + 4 * u]);
+        const float4 f4l = *reinterpret_cast<const float4*>(&cL[cb + 4 * u]);
+        const float fs[4] = {f4s.x, f4s.y, f4s.z, f4s.w}, fl[4] = {f4l.x, f4l.y, f4l.z, f4l.w};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-        if (lane == 0) colsum[qd][col] = cs;
-        m4[e] = __expf(x) * pq;
-        m5[e] = __expf(-x) * pk;
+        for (int e4 = 0; e4 < 4; ++e4) {
+          const int e = 4 * u + e4;
+          const float x = gv[e];
+          const float pq = fmaf(fs[e4], m2[e], m4[e]);  // dq = e^{x} pq
+          const float lm3 = fl[e4] * m3[e];
+          const float pk = m5[e] + lm3;                 // dk = e^{-x} pk
+          gv[e] = qv[e] * pq - kv[e] * pk;              // dg_raw = q dq - k dk
+          cs[e] = kv[e] * lm3;                          // (e^{GL-G} dki) k
+          m4[e] = __expf(x) * pq;
+          m5[e] = __expf(-x) * pk;
+        }
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<float4*>(gp + ptx::sw128(i, (cb & 31) * 4 + u * 16)) =
+            make_float4(gv[4 * u], gv[4 * u + 1], gv[4 * u + 2], gv[4 * u + 3]);
+      uint32_t dqw[8], dkw[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         dqw[u] = ptx::pack_bf16(m4[2 * u], m4[2 * u + 1]);
         dkw[u] = ptx::pack_bf16(m5[2 * u], m5[2 * u + 1]);
       }
-      // stage [128 rows][128 cols] bf16 as two 128B-swizzled [128][64] tiles each
-      unsigned char* tq = dqs + (cb >> 6) * TILE_BYTES;
-      unsigned char* tk = dAs + (cb >> 6) * TILE_BYTES;
-      const uint32_t by = (uint32_t)(cb & 63) * 2;
-      *reinterpret_cast<uint4*>(tq + ptx::sw128(i, by)) = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
-      *reinterpret_cast<uint4*>(tq + ptx::sw128(i, by + 16)) = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
-      *reinterpret_cast<uint4*>(tk + ptx::sw128(i, by)) = make_uint4(dkw[0], dkw[1], dkw[2], dkw[3]);
-      *reinterpret_cast<uint4*>(tk + ptx::sw128(i, by + 16)) = make_uint4(dkw[4], dkw[5], dkw[6], dkw[7]);
+      *reinterpret_cast<uint4*>(qtl + qb) = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
+      *reinterpret_cast<uint4*>(qtl + qb2) = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
+      *reinterpret_cast<uint4*>(ktl + qb) = make_uint4(dkw[0], dkw[1], dkw[2], dkw[3]);
+      *reinterpret_cast<uint4*>(ktl + qb2) = make_uint4(dkw[4], dkw[5], dkw[6], dkw[7]);
+      const float tot = dqk_reduce16(cs, lane);
+      if ((lane & 1) == 0) colsum[qd][cb + dqk_red_col(lane)] = tot;
     }
   }
   ptx::fence_async_smem();
-  ptx::tc_fence_before();
   __syncthreads();
   if (tid == 0 && ok) {  // dq, dk tiles -> global (rows past T are clipped by the tensor map)
-    ptx::tma_store_4d(&maps.dq, k0, h, row0, b, dqs);
-    ptx::tma_store_4d(&maps.dq, k0 + 64, h, row0, b, dqs + TILE_BYTES);
-    ptx::tma_store_4d(&maps.dk, k0, h, row0, b, dAs);
-    ptx::tma_store_4d(&maps.dk, k0 + 64, h, row0, b, dAs + TILE_BYTES);
+    ptx::tma_store_4d(&maps.dq, k0, h, row0, b, qtl);
+    ptx::tma_store_4d(&maps.dk, k0, h, row0, b, ktl);
     ptx::bulk_commit();
   }
-  // ---------------- dg = reverse cumsum over rows + inter term: 2 threads per column ----------------
-  const int col = tid & 127, half = tid >> 7;
-  const unsigned char* gt = Gs + (col >> 5) * TILE_BYTES;
-  const uint32_t by = (uint32_t)(col & 31) * 4;
-  if (ok && half == 1) {
-    float tsum = 0.f;
-    for (int r = 64; r < 128; ++r) tsum += *reinterpret_cast<const float*>(gt + ptx::sw128(r, by));
-    dgtot[col] = tsum;
+  // ---------------- dg = reverse cumsum over rows + inter term, in place, then one TMA store ----------------
+  float dv[32];
+  if (ok) {
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      dv[r] = *reinterpret_cast<const float*>(gt + ptx::sw128(seg * 32 + r, gby));
+      sum += dv[r];
+    }
+    segs[seg][gcol] = sum;
   }
   __syncthreads();
   if (ok) {
-    const float inter = __expf(GLs[col]) * hdh2[0][col] + colsum[0][col] + colsum[1][col] + colsum[2][col] +
-                        colsum[3][col];
-    float run = half ? 0.f : dgtot[col];
-    for (int r = half * 64 + 63; r >= half * 64; --r) {
-      run += *reinterpret_cast<const float*>(gt + ptx::sw128(r, by));
-      if (row0 + r < p.T) p.dg[((size_t)(b * p.T + row0 + r) * p.H + h) * p.K + k0 + col] = run + inter;
+    float run = cGL[gcol] * (hdh2[0][gcol] + hdh2[1][gcol]) + colsum[0][gcol] + colsum[1][gcol] + colsum[2][gcol] +
+                colsum[3][gcol];
+    for (int s2 = seg + 1; s2 < 4; ++s2) run += segs[s2][gcol];
+#pragma unroll
+    for (int r = 31; r >= 0; --r) {
+      run += dv[r];
+      *reinterpret_cast<float*>(gt + ptx::sw128(seg * 32 + r, gby)) = run;
     }
+  }
+  ptx::fence_async_smem();
+  __syncthreads();
+  if (tid == 0 && ok) {
+    ptx::tma_store_4d(&maps.dg, k0, h, row0, b, Gs);
+    ptx::tma_store_4d(&maps.dg, k0 + 32, h, row0, b, Gs + TILE_BYTES);
+    ptx::bulk_commit();
   }
   if (!ok && tid == 0) {  // drain loads that may still be in flight (bounded)
     ptx::mbar_wait(&full[0], 0);
     ptx::mbar_wait(&full[1], 0);
-    ptx::mbar_wait(&bar_qk, 0);
+    ptx::mbar_wait(&bar_g, 0);
+    ptx::mbar_wait(&bar_q, 0);
+    ptx::mbar_wait(&bar_k, 0);
   }
-  if (tid == 0) ptx::bulk_wait<0>();
+  if (tid == 0) ptx::bulk_wait_read<0>();  // the stores have read the staging tiles
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
+  if (warp == 0) ptx::tmem_dealloc(tmem_base, 256);
 }
 
 TOPS_DEVICE_ERROR_READER(read_device_error)
@@ -1067,7 +1128,7 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   return TOPS_OK;
 }
 
-static size_t dqk_smem() { return 2 * 4 * (size_t)TILE_BYTES + 4 * (size_t)TILE_BYTES + 1024; }
+static size_t dqk_smem() { return 2 * (size_t)DQK_STG + 1024; }
 
 size_t bwd_workspace(const tops_gla_shape& s, bool have_saved) {
   const int NTb = (s.T + BT - 1) / BT;
@@ -1104,9 +1165,9 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   DqkMaps dm;
   okm = okm && map_tok(&dm.dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
         map_tok(&dm.v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
-        map_state(&dm.hs, sv.h, s.B * NTb * s.H, s.K, s.V, 128) &&
-        map_state(&dm.dhs, dhs, s.B * NTb * s.H, s.K, s.V, 128) &&
-        map_tok(&dm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+        map_state(&dm.hs, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
+        map_state(&dm.dhs, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
+        map_tok(&dm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.dg, dg, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_tok(&dm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm.dq, dq, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
@@ -1131,7 +1192,10 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     LaunchTimer lt(st, "tc_dqk");
     DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
     if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
-    k_dqk<<<dim3(s.K / 128, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
+    // two CTAs per SM need the largest shared-memory carveout
+    if ((e = cudaFuncSetAttribute(k_dqk, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+      return cuda_status(e, "tc dqk carveout");
+    k_dqk<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
     TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
   }
   return TOPS_OK;
