@@ -128,7 +128,7 @@ struct PrepMaps {
   CUtensorMap q, k, g, qh, kd, A;
 };
 
-__global__ void __launch_bounds__(256, 1) k_prep(const __grid_constant__ PrepMaps maps, PrepParams p) {
+__global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMaps maps, PrepParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* qb = smem;                   // [128][64] bf16: q -> qhat (in place)
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(256, 1) k_prep(const __grid_constant__ PrepMap
   unsigned char* gb = kb + TILE_BYTES;        // 2 x [128][32] fp32
   unsigned char* qt = gb + 2 * TILE_BYTES;    // q e^{G-Gm}
   unsigned char* kt = qt + TILE_BYTES;        // k e^{Gm-G}
-  __shared__ float psum[4][64];
+  __shared__ __align__(16) float wtot[8][64];  // per-warp column sums of g
   __shared__ __align__(8) uint64_t bar_load, bar_mma;
   __shared__ uint32_t tmem_base;
 
@@ -160,8 +160,11 @@ __global__ void __launch_bounds__(256, 1) k_prep(const __grid_constant__ PrepMap
   const uint32_t tacc = tmem_base;
   constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, false, false);
 
-  // gating thread mapping: part (32 rows) x column (64 per K block)
-  const int part = warp >> 1, col = (warp & 1) * 32 + lane;
+  // gating thread mapping: warp w owns rows w*16 .. w*16+15; lane = (row quad sub, 8-column chunk c)
+  const int c8 = lane & 7, sub = lane >> 3, r0 = warp * 16 + sub * 4;
+  // fp32 g: chunk c8 lives in tile c8/4 at byte (c8%4)*32; chunks 4..7 read their two 16-byte
+  // halves in the opposite order so each 8-lane access phase touches 8 different bank groups
+  const uint32_t go0 = (uint32_t)(c8 & 3) * 32 + ((c8 >> 2) ? 16u : 0u);
   bool ok = true;
   for (int kbi = 0; kbi < nkb && ok; ++kbi) {
     if (tid == 0) {
@@ -171,31 +174,98 @@ __global__ void __launch_bounds__(256, 1) k_prep(const __grid_constant__ PrepMap
       ptx::tma_load_4d(kb, &maps.k, kbi * 64, h, row0, b, &bar_load);
       ptx::tma_load_4d(gb, &maps.g, kbi * 64, h, row0, b, &bar_load);
       ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, kbi * 64 + 32, h, row0, b, &bar_load);
+      if (kbi + 1 < nkb) {  // the next K block into L2 while this one is gated
+        ptx::tma_prefetch_4d(&maps.q, kbi * 64 + 64, h, row0, b);
+        ptx::tma_prefetch_4d(&maps.k, kbi * 64 + 64, h, row0, b);
+        ptx::tma_prefetch_4d(&maps.g, kbi * 64 + 64, h, row0, b);
+        ptx::tma_prefetch_4d(&maps.g, kbi * 64 + 96, h, row0, b);
+      }
     }
     ok = ptx::mbar_wait(&bar_load, (uint32_t)(kbi & 1));
     if (!ok) break;
-    // g(row, col): fp32 tile (col / 32), byte (col % 32) * 4
-    const unsigned char* gt = gb + (col >> 5) * TILE_BYTES;
-    const uint32_t gbyte = (uint32_t)(col & 31) * 4;
-    float s = 0.f;
-    for (int r = part * 32; r < part * 32 + 32; ++r) s += *reinterpret_cast<const float*>(gt + ptx::sw128(r, gbyte));
-    psum[part][col] = s;
+    const unsigned char* gt = gb + (c8 >> 2) * TILE_BYTES;
+    float gv[4][8], ps[8];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      float4 lo = *reinterpret_cast<const float4*>(gt + ptx::sw128(r0 + rr, go0));
+      float4 hi = *reinterpret_cast<const float4*>(gt + ptx::sw128(r0 + rr, go0 ^ 16u));
+      if (c8 >> 2) {
+        const float4 t = lo;
+        lo = hi;
+        hi = t;
+      }
+      gv[rr][0] = lo.x; gv[rr][1] = lo.y; gv[rr][2] = lo.z; gv[rr][3] = lo.w;
+      gv[rr][4] = hi.x; gv[rr][5] = hi.y; gv[rr][6] = hi.z; gv[rr][7] = hi.w;
+    }
+    // inclusive scan over the 4 row quads of this warp (lanes 8 apart), then warp totals
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float own = gv[0][j] + gv[1][j] + gv[2][j] + gv[3][j];
+      float v = own, t = __shfl_up_sync(0xffffffffu, v, 8);
+      if (sub >= 1) v += t;
+      t = __shfl_up_sync(0xffffffffu, v, 16);
+      if (sub >= 2) v += t;
+      ps[j] = v - own;  // sum of this warp's rows above this quad
+      if (sub == 3) wtot[warp][c8 * 8 + j] = v;
+    }
     __syncthreads();
-    float off = 0.f;
-    for (int pp = 0; pp < part; ++pp) off += psum[pp][col];
-    const float GL = psum[0][col] + psum[1][col] + psum[2][col] + psum[3][col];
-    const float Gm = psum[0][col] + psum[1][col];
-    const float eGm = __expf(Gm), eGLm = __expf(GL - Gm);
-    if (part == 0) p.D[((size_t)(b * p.NTb + c) * p.H + h) * p.K + kbi * 64 + col] = __expf(GL);
-    float run = off;
-    for (int r = part * 32; r < part * 32 + 32; ++r) {
-      run += *reinterpret_cast<const float*>(gt + ptx::sw128(r, gbyte));
-      const float a = __expf(run - Gm), bb = __expf(Gm - run);
-      const float qv = bf(qb, r, col), kv = bf(kb, r, col);
-      st_bf(qt, r, col, qv * a);
-      st_bf(kt, r, col, kv * bb);
-      st_bf(qb, r, col, p.scale * qv * a * eGm);
-      st_bf(kb, r, col, kv * bb * eGLm);
+    float off[8], gm[8], gl[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      off[j] = ps[j];
+      gm[j] = 0.f;
+      gl[j] = 0.f;
+    }
+#pragma unroll
+    for (int w2 = 0; w2 < 8; ++w2) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&wtot[w2][c8 * 8]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&wtot[w2][c8 * 8 + 4]);
+      const float t8[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (w2 < warp) off[j] += t8[j];
+        if (w2 < 4) gm[j] += t8[j];  // rows 0..63: Gm is G at row 63
+        gl[j] += t8[j];
+      }
+    }
+    float sq[8], sk[8];  // scale e^{Gm}, e^{GL-Gm}
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sq[j] = p.scale * __expf(gm[j]);
+      sk[j] = __expf(gl[j] - gm[j]);
+    }
+    if (warp == 0 && sub == 0) {
+      float* dp = p.D + ((size_t)(b * p.NTb + c) * p.H + h) * p.K + kbi * 64 + c8 * 8;
+      reinterpret_cast<float4*>(dp)[0] = make_float4(__expf(gl[0]), __expf(gl[1]), __expf(gl[2]), __expf(gl[3]));
+      reinterpret_cast<float4*>(dp)[1] = make_float4(__expf(gl[4]), __expf(gl[5]), __expf(gl[6]), __expf(gl[7]));
+    }
+    float run[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) run[j] = off[j] - gm[j];  // running G - Gm
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const uint32_t o = ptx::sw128(r0 + rr, c8 * 16);
+      uint4 xq = *reinterpret_cast<const uint4*>(qb + o), xk = *reinterpret_cast<const uint4*>(kb + o);
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&xq);
+      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&xk);
+      uint32_t wqt[4], wkt[4], wqh[4], wkd[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = __bfloat1622float2(q2[e]), fk = __bfloat1622float2(k2[e]);
+        run[2 * e] += gv[rr][2 * e];
+        run[2 * e + 1] += gv[rr][2 * e + 1];
+        const float a0 = __expf(run[2 * e]), a1 = __expf(run[2 * e + 1]);
+        const float b0 = __expf(-run[2 * e]), b1 = __expf(-run[2 * e + 1]);
+        const float qt0 = fq.x * a0, qt1 = fq.y * a1, kt0 = fk.x * b0, kt1 = fk.y * b1;
+        wqt[e] = ptx::pack_bf16(qt0, qt1);
+        wkt[e] = ptx::pack_bf16(kt0, kt1);
+        wqh[e] = ptx::pack_bf16(qt0 * sq[2 * e], qt1 * sq[2 * e + 1]);
+        wkd[e] = ptx::pack_bf16(kt0 * sk[2 * e], kt1 * sk[2 * e + 1]);
+      }
+      *reinterpret_cast<uint4*>(qt + o) = make_uint4(wqt[0], wqt[1], wqt[2], wqt[3]);
+      *reinterpret_cast<uint4*>(kt + o) = make_uint4(wkt[0], wkt[1], wkt[2], wkt[3]);
+      *reinterpret_cast<uint4*>(qb + o) = make_uint4(wqh[0], wqh[1], wqh[2], wqh[3]);
+      *reinterpret_cast<uint4*>(kb + o) = make_uint4(wkd[0], wkd[1], wkd[2], wkd[3]);
     }
     ptx::fence_async_smem();
     ptx::tc_fence_before();
@@ -862,9 +932,17 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
   if (ok) {
     for (int it = tid; it < 128 * 8; it += 256) {
       const int chunk = it & 7, row = it >> 3, col0 = chunk * 8;
+      // chunks 4..7 (second fp32 tile) read their two halves in the opposite order, so the
+      // eight lanes of each 16-byte access phase hit eight different bank groups
       const unsigned char* gp = Gs + (col0 >> 5) * TILE_BYTES;
-      const float4 ga = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, (col0 & 31) * 4));
-      const float4 gb = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, (col0 & 31) * 4 + 16));
+      const uint32_t o0 = (col0 & 31) * 4 + ((chunk >> 2) ? 16u : 0u);
+      float4 ga = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, o0));
+      float4 gb = *reinterpret_cast<const float4*>(gp + ptx::sw128(row, o0 ^ 16u));
+      if (chunk >> 2) {
+        const float4 t = ga;
+        ga = gb;
+        gb = t;
+      }
       const float x8[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
       uint4* pq = reinterpret_cast<uint4*>(qtl + ptx::sw128(row, chunk * 16));
       uint4* pk = reinterpret_cast<uint4*>(ktl + ptx::sw128(row, chunk * 16));
@@ -1106,6 +1184,8 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     LaunchTimer lt(st, "tc_prep");
     PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
     if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
+    if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+      return cuda_status(e, "tc prep carveout");
     k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
     TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   }
