@@ -322,14 +322,22 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
 }
 
 // ===========================================================================
-// k_scan: state scan over chunks.  grid (V/128, H, B), 256 threads.
+// k_scan: state scan over chunks.  grid (V/128, H, B * nspan), 256 threads.
+// Long sequences with few (batch, head, V-tile) units are split into nspan spans of
+// span_len chunks that scan in parallel: a first launch runs every span from a zero
+// state (no chunk states stored) and returns its final state and the product of its
+// chunk decays; k_span_prefix chains those into each span's incoming state
+// (H_{s+1} = P_s H_s + E_s, the scan is linear in its initial state); a second launch
+// re-runs every span from its incoming state and stores the chunk states.
 // ===========================================================================
 struct ScanParams {
   int B, T, H, K, V, NTb, reverse;
   const float* D;     // [B*NTb, H, K]
-  const float* init;  // [B, H, K, V] fp32 or null
-  float* fin;         // [B, H, K, V] fp32 or null
+  const float* init;  // [nspan][B, H, K, V] fp32 (span s starts from init[s]) or null (zero)
+  float* fin;         // fin_mode 0: [nspan][B, H, K, V] every span's final state; 1: [B, H, K, V] last span only
   bf16* states;       // [B*NTb, H, K, V] bf16 (chunk-start states) or null
+  int nspan, span_len, fin_mode;
+  float* span_decay;  // [nspan][B, H, K] product of each span's chunk decays, or null
 };
 
 struct ScanMaps {
@@ -352,8 +360,11 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   __shared__ __align__(8) uint64_t bar_full[2], bar_mma;
   __shared__ uint32_t tmem_base;
 
-  const int vt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int vt = blockIdx.x, h = blockIdx.y, b = blockIdx.z / p.nspan, sp_ = blockIdx.z % p.nspan;
   const int v0 = vt * BV;
+  const int i0 = sp_ * p.span_len;                      // first iteration of this span
+  const int n_it = min(p.span_len, p.NTb - i0);         // iterations (chunks) of this span
+  const size_t span_off = (size_t)sp_ * p.B * p.H * p.K * p.V;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = warp & 3, hf = warp >> 2;  // lane quadrant, state half handled by this warp
   const int krow = hf * 128 + qd * 32 + lane;
@@ -378,7 +389,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   auto sbuf = [&](int i) { return tmem_base + (uint32_t)((i & 1) * 256); };
   constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, true, true);
 
-  auto chunk_of = [&](int i) { return p.reverse ? p.NTb - 1 - i : i; };
+  auto chunk_of = [&](int i) { return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i; };
   auto issue = [&](int i) {
     const int c = chunk_of(i);
     unsigned char* buf = smem + (i & 1) * buf_bytes;
@@ -389,7 +400,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   };
   if (tid == 0) {
     issue(0);
-    if (p.NTb > 1) issue(1);
+    if (n_it > 1) issue(1);
   }
   // initial state -> TMEM buffer 0
   if (active) {
@@ -398,7 +409,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[srow + cb * 32 + j] : 0.f;
+      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[span_off + srow + cb * 32 + j] : 0.f;
       ptx::tmem_st32(tmem_lane_addr(sbuf(0), qd * 32, hf * 128 + cb * 32), r);
     }
     ptx::tmem_st_wait();
@@ -406,18 +417,19 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   bool ok = true;
   // the decay of chunk i+1 is fetched one iteration ahead (its latency hides behind chunk i)
   auto decay_of = [&](int i) {
-    return active && i < p.NTb ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
+    return active && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
   };
-  float d_next = decay_of(0);
-  for (int i = 0; i < p.NTb; ++i) {
+  float d_next = decay_of(0), dprod = 1.f;
+  for (int i = 0; i < n_it; ++i) {
     const int c = chunk_of(i);
     const float d = d_next;
+    dprod *= d;
     d_next = decay_of(i + 1);
     if (i > 0) {
       ok = ptx::mbar_wait(&bar_mma, (uint32_t)((i - 1) & 1));
       ptx::tc_fence_after();
       if (!ok) break;
-      if (tid == 0 && i + 1 < p.NTb) issue(i + 1);  // buffer (i+1)&1 was read by chunk i-1, now complete
+      if (tid == 0 && i + 1 < n_it) issue(i + 1);  // buffer (i+1)&1 was read by chunk i-1, now complete
     }
     // pass A: next-state buffer <- D_c * h_c (h_c stays untouched in its buffer)
     if (active) {
@@ -485,14 +497,16 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     }
     // a failed wait in thread 0 leaves bar_mma pending: the next wait times out for everyone
   }
-  if (ok) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((p.NTb - 1) & 1));
+  if (ok) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
   ptx::tc_fence_after();
-  if (ok && active && p.fin) {
-    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0;
+  if (ok && active && p.span_decay && vt == 0)
+    p.span_decay[((size_t)(sp_ * p.B + b) * p.H + h) * p.K + krow] = dprod;
+  if (ok && active && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
+    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
-      ptx::tmem_ld32(tmem_lane_addr(sbuf(p.NTb), qd * 32, hf * 128 + cb * 32), r);
+      ptx::tmem_ld32(tmem_lane_addr(sbuf(n_it), qd * 32, hf * 128 + cb * 32), r);
       ptx::tmem_ld_wait();
       float4* dst = reinterpret_cast<float4*>(p.fin + srow + cb * 32);
 #pragma unroll
@@ -508,6 +522,24 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
+}
+
+// Incoming state of every span: H_0 = init (or 0), H_{s+1} = P_s * H_s + E_s (fp32, per
+// element; P is per state row).  One thread per 4 consecutive state columns.
+__global__ void k_span_prefix(int S, int B, int H, int K, int V, const float* __restrict__ init,
+                              const float* __restrict__ P, const float* __restrict__ E, float* __restrict__ Hs) {
+  const size_t n4 = (size_t)B * H * K * V / 4;
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n4) return;
+  const size_t e = idx * 4, per = (size_t)B * H * K * V;
+  const size_t row = e / V;  // (b*H + h)*K + k
+  float4 cur = init ? reinterpret_cast<const float4*>(init)[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < S; ++s) {
+    reinterpret_cast<float4*>(Hs + s * per)[idx] = cur;
+    const float d = P[s * (size_t)B * H * K + row];
+    const float4 x = reinterpret_cast<const float4*>(E + s * per)[idx];
+    cur = make_float4(fmaf(d, cur.x, x.x), fmaf(d, cur.y, x.y), fmaf(d, cur.z, x.z), fmaf(d, cur.w, x.w));
+  }
 }
 
 // ===========================================================================
@@ -1114,6 +1146,47 @@ static int sm_count() {
   return n;
 }
 
+// Span split of the state scans: enough spans that the scan grid fills the SMs (one CTA
+// per SM: 512 TMEM columns), at least 16 chunks per span; one span when the (batch, head,
+// V-tile) units alone fill half the GPU or the sequence is short.
+struct Spans {
+  int n, len;
+};
+static Spans spans_for(const tops_gla_shape& s, int NTb) {
+  const int units = (s.V / BV) * s.H * s.B;
+  const int nsm = sm_count();
+  Spans r{1, NTb};
+  if (units * 2 > nsm || NTb < 32) return r;
+  int S = nsm / units;
+  if (S > NTb / 16) S = NTb / 16;
+  if (S < 2) return r;
+  r.len = (NTb + S - 1) / S;
+  r.n = (NTb + r.len - 1) / r.len;
+  return r;
+}
+
+// scratch of a span-split scan: final states E and incoming states Hs [nspan][B,H,K,V],
+// span decays P [nspan][B,H,K] (fp32); bytes from `off` (1 KB aligned pieces)
+struct SpanBufs {
+  float *E = nullptr, *Hs = nullptr, *P = nullptr;
+};
+static size_t carve_spans(const tops_gla_shape& s, Spans spn, char* base, size_t off, SpanBufs* out) {
+  if (spn.n <= 1) return off;
+  auto take = [&](size_t bytes) {
+    off = (off + 1023) & ~size_t(1023);
+    char* p = base ? base + off : nullptr;
+    off += bytes;
+    return reinterpret_cast<float*>(p);
+  };
+  const size_t st = (size_t)spn.n * s.B * s.H * s.K * s.V * 4;
+  SpanBufs b;
+  b.E = take(st);
+  b.Hs = take(st);
+  b.P = take((size_t)spn.n * s.B * s.H * s.K * 4);
+  if (out) *out = b;
+  return off;
+}
+
 bool eligible(const tops_gla_shape& s) {
   return s.dtype == TOPS_BF16 && s.cu_seqlens == nullptr && (s.K == 128 || s.K == 256) && s.V % BV == 0 &&
          s.T > 0 && s.B > 0 && s.H > 0 && tops_gla_has_tcgen05() && encode_fn() != nullptr;
@@ -1123,6 +1196,7 @@ bool eligible(const tops_gla_shape& s) {
 struct Saved {
   bf16 *qh, *kd, *A, *h;
   float* D;
+  SpanBufs sb;  // scratch of a span-split forward scan (empty when the scan runs in one span)
 };
 
 static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
@@ -1141,6 +1215,7 @@ static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
   v.A = reinterpret_cast<bf16*>(take(tok * BT * 2));
   v.D = reinterpret_cast<float*>(take((size_t)s.B * NTb * s.H * s.K * 4));
   v.h = reinterpret_cast<bf16*>(take((size_t)s.B * NTb * s.H * s.K * s.V * 2));
+  off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb);
   if (sv) *sv = v;
   return off;
 }
@@ -1154,6 +1229,40 @@ static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 2 * TILE_BY
 template <typename KernelT>
 static cudaError_t set_smem(KernelT k, size_t bytes) {
   return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// One state scan (forward h or reverse dh), split into spans when that fills the GPU.
+static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, const float* D, const float* init,
+                    float* fin, bf16* states, const SpanBufs& sb, Spans spn, cudaStream_t st, const char* name) {
+  const int NTb = (s.T + BT - 1) / BT;
+  cudaError_t e;
+  if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  if (spn.n <= 1) {
+    LaunchTimer lt(st, name);
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr};
+    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK(name);
+    return TOPS_OK;
+  }
+  {
+    LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P};
+    k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
+  }
+  {
+    LaunchTimer lt(st, "tc_span_prefix");
+    const size_t n4 = (size_t)s.B * s.H * s.K * s.V / 4;
+    k_span_prefix<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, init, sb.P, sb.E, sb.Hs);
+    TOPS_CUDA_LAUNCH_CHECK("tc_span_prefix");
+  }
+  {
+    LaunchTimer lt(st, name);
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr};
+    k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK(name);
+  }
+  return TOPS_OK;
 }
 
 // Forward: o, ht and (in `saved`) qhat, kdec, A, D, chunk-start states h.
@@ -1189,13 +1298,8 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
     TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   }
-  {
-    LaunchTimer lt(st, "tc_scan");
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, 0, sv.D, h0, ht, sv.h};
-    if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
-    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
-    TOPS_CUDA_LAUNCH_CHECK("tc_scan");
-  }
+  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, "tc_scan");
+  if (rc) return rc;
   {
     LaunchTimer lt(st, "tc_out");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 0, static_cast<bf16*>(o)};
@@ -1213,6 +1317,7 @@ static size_t dqk_smem() { return 2 * (size_t)DQK_STG + 1024; }
 size_t bwd_workspace(const tops_gla_shape& s, bool have_saved) {
   const int NTb = (s.T + BT - 1) / BT;
   size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);  // dh states
+  n = (carve_spans(s, spans_for(s, NTb), nullptr, n, nullptr) + 1023) & ~size_t(1023);
   if (!have_saved) n += saved_bytes(s);
   return n;
 }
@@ -1225,10 +1330,13 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   char* ws = static_cast<char*>(workspace);
   bf16* dhs = reinterpret_cast<bf16*>(ws);
   const size_t dh_bytes = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
+  const Spans spn = spans_for(s, NTb);
+  SpanBufs sb;
+  const size_t span_end = (carve_spans(s, spn, ws, dh_bytes, &sb) + 1023) & ~size_t(1023);
   void* saved = const_cast<void*>(saved_in);
   int rc;
   if (saved == nullptr) {  // recompute the forward intermediates (o is discarded into dv's buffer)
-    saved = ws + dh_bytes;
+    saved = ws + span_end;
     if ((rc = fwd(s, q, k, v, g, h0, dv, nullptr, saved, st))) return rc;
   }
   Saved sv;
@@ -1252,13 +1360,7 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
         map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
-  {
-    LaunchTimer lt(st, "tc_scan_bwd");
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, 1, sv.D, dht, dh0, dhs};
-    if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
-    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
-    TOPS_CUDA_LAUNCH_CHECK("tc_scan_bwd");
-  }
+  if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, "tc_scan_bwd"))) return rc;
   {
     LaunchTimer lt(st, "tc_out_dv");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 1, static_cast<bf16*>(dv)};

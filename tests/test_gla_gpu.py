@@ -362,6 +362,9 @@ TC_CASES = [
     dict(B=2, T=640, H=2, K=256, V=512, seed=41),
     dict(B=1, T=333, H=3, K=128, V=256, seed=42, h0=True),
     dict(B=3, T=129, H=1, K=256, V=128, seed=43, h0=True),
+    # few (batch, head, V-tile) units and many chunks: the state scans split into spans
+    dict(B=1, T=4173, H=2, K=128, V=128, seed=47, h0=True, dht=True),
+    dict(B=1, T=16384, H=1, K=128, V=256, seed=48, h0=True),
 ]
 
 
@@ -415,4 +418,28 @@ def test_tc_backward_vs_oracle(gla, case):
     if h0t is not None:
         assert_rel_l2("dh0", h0t.grad, dh0_r, BF16_L2)
     torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
+
+
+def test_tc_long_sequence_takes_the_span_split_scan(gla):
+    """A long single sequence (2 units, 128 chunks) runs its state scans as parallel spans."""
+    from tops import _C
+    from tops.ops.gla import _core
+    torch.manual_seed(0)
+    B, T, H, K, V = 1, 16384, 1, 128, 256
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, T, H, K, device="cuda", dtype=bf) for _ in range(2))
+    v = torch.randn(B, T, H, V, device="cuda", dtype=bf)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device="cuda")) / 16).contiguous()
+    do = torch.randn(B, T, H, V, device="cuda", dtype=bf)
+    p = _core.make_plan(q, V, 64, None, K ** -0.5)
+    _C.timing_enable(True)
+    try:
+        o, ht, sv = _core.chunk_fwd(p, q, k, v, g, None, True, save=True)
+        _core.chunk_bwd(p, q, k, v, g, None, do, None, block=sv.get("block"), want_dh0=True)
+        torch.cuda.synchronize()
+    finally:
+        _C.timing_enable(False)
+    names = {n for n, _ in _C.timing_collect()}
+    assert {"tc_scan_span", "tc_span_prefix", "tc_scan", "tc_scan_bwd_span", "tc_scan_bwd"} <= names, names
     assert _C.lib().tops_gla_device_error() == 0
