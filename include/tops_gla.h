@@ -103,7 +103,7 @@ typedef struct tops_gla_chunk_fwd_args {
   const void* q; const void* k; const void* v;
   const float* g;              /* [B,T,H,K] log-space gates, NULL = no decay */
   const float* h0;             /* [N,H,K,V] or NULL */
-  void* o;                     /* out [B,T,H,V] (dtype) */
+  void* o;                     /* out [B,T,H,V] (dtype); NULL = final state only (ht required) */
   float* ht;                   /* out [N,H,K,V] or NULL (output_final_state=False) */
   /* Optional saved intermediates for the backward (reference chunk_gla_fwd
    * returns (g_cumsum, A, h, ht, o), tops/ops/gla/chunk.py:1083-1179).  NULL = not
@@ -120,7 +120,9 @@ typedef struct tops_gla_chunk_fwd_args {
 
 /* Chunked GLA forward: o = chunk_gla(q,k,v,g,scale,h0)[0], ht = final state.
  * Replaces tops.ops.gla.chunk_gla / chunk_gla_fwd (tops/ops/gla/chunk.py:1187,1083)
- * and fused_chunk_gla (tops/ops/gla/fused_chunk.py:4). */
+ * and fused_chunk_gla (tops/ops/gla/fused_chunk.py:4).  With o == NULL only the
+ * final state is computed (the state scan without the output GEMM): the first pass
+ * of a sequence-parallel forward, whose span states are exchanged between ranks. */
 TOPS_API int tops_gla_chunk_fwd(const tops_gla_chunk_fwd_args* a, void* stream);
 TOPS_API size_t tops_gla_chunk_fwd_workspace_size(const tops_gla_chunk_fwd_args* a);
 /* Bytes of the forward's saved block for this problem; 0 when the problem runs on
@@ -137,7 +139,7 @@ typedef struct tops_gla_chunk_bwd_args {
   const float* g_cumsum;       /* optional saved fwd intermediates (NULL = recompute) */
   const float* A;
   const float* h;
-  void* dq; void* dk; void* dv;/* out (dtype) */
+  void* dq; void* dk; void* dv;/* out (dtype); all four gradients NULL = dh0 only */
   float* dg;                   /* out [B,T,H,K] fp32 */
   float* dh0;                  /* out [N,H,K,V] or NULL */
   void* workspace; size_t workspace_bytes;
@@ -146,7 +148,9 @@ typedef struct tops_gla_chunk_bwd_args {
 
 /* Chunked GLA backward -> dq, dk, dv, dg, dh0.
  * Replaces tops.ops.gla.chunk_gla_bwd (tops/ops/gla/chunk.py:815) and
- * chunk_gla_bwd_with_pl (tops/ops/gla/chunk.py:980). */
+ * chunk_gla_bwd_with_pl (tops/ops/gla/chunk.py:980).  With dq, dk, dv and dg all
+ * NULL only dh0 is computed (the reverse state scan): the first pass of a
+ * sequence-parallel backward. */
 TOPS_API int tops_gla_chunk_bwd(const tops_gla_chunk_bwd_args* a, void* stream);
 
 /* Chunked GLA forward that allocates nothing and needs no workspace.  No counterpart

@@ -166,7 +166,7 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
       *ws_need = own ? 0 : need_saved;
       return TOPS_OK;
     }
-    TOPS_CHECK_ARG(a->q && a->k && a->v && a->o, "chunk_fwd: q, k, v and o are required");
+    TOPS_CHECK_ARG(a->q && a->k && a->v && (a->o || a->ht), "chunk_fwd: q, k, v and o (or ht) are required");
     void* blk = own ? a->saved : a->workspace;
     if (!own && (a->workspace == nullptr || a->workspace_bytes < need_saved))
       return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: workspace smaller than tops_gla_chunk_fwd_workspace_size()");
@@ -174,7 +174,7 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
   }
   if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {
-    TOPS_CHECK_ARG(a->q && a->k && a->v && a->o, "chunk_fwd: q, k, v and o are required");
+    TOPS_CHECK_ARG(a->q && a->k && a->v && (a->o || a->ht), "chunk_fwd: q, k, v and o (or ht) are required");
   }
   Carve cv(dry ? nullptr : a->workspace);
   float* gc = a->g_cumsum ? a->g_cumsum : cv.take<float>(tok_elems(s, s.K));
@@ -195,6 +195,7 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
     note_launch(1);
   }
   if ((rc = simt::fwd_h(s, a->k, a->v, gc, a->h0, h, a->ht, st))) return rc;
+  if (a->o == nullptr) return TOPS_OK;  // final state only
   if ((rc = simt::fwd_intra(s, a->q, a->k, gc, 1, A, st))) return rc;
   return simt::fwd_o(s, a->q, a->v, gc, A, h, a->o, st);
 }
@@ -211,6 +212,8 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
   if (rc) return rc;
   const tops_gla_shape& s = a->s;
   const bool dry = ws_need != nullptr;
+  // dh0 only (no gradient outputs): the reverse state scan alone
+  const bool dh0_only = !a->dq && !a->dk && !a->dv && !a->dg;
   if (use_tc_bwd(a)) {
     const bool have = a->saved != nullptr;
     if (have && a->saved_bytes < tc::saved_bytes(s))
@@ -220,8 +223,8 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
       *ws_need = need;
       return TOPS_OK;
     }
-    TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && a->dq && a->dk && a->dv && a->dg,
-                   "chunk_bwd: q, k, v, do, dq, dk, dv and dg are required");
+    TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && ((a->dq && a->dk && a->dv && a->dg) || (dh0_only && a->dh0)),
+                   "chunk_bwd: q, k, v, do and dq, dk, dv, dg (or dh0 alone) are required");
     if (a->workspace == nullptr || a->workspace_bytes < need)
       return fail(TOPS_ERR_WORKSPACE, "chunk_bwd: workspace smaller than tops_gla_chunk_bwd_workspace_size()");
     return tc::bwd(s, a->q, a->k, a->v, a->g, a->h0, a->do_, a->dht, a->saved, a->dq, a->dk, a->dv, a->dg, a->dh0,
@@ -229,8 +232,8 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
   }
   if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {
-    TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && a->dq && a->dk && a->dv && a->dg,
-                   "chunk_bwd: q, k, v, do, dq, dk, dv and dg are required");
+    TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && ((a->dq && a->dk && a->dv && a->dg) || (dh0_only && a->dh0)),
+                   "chunk_bwd: q, k, v, do and dq, dk, dv, dg (or dh0 alone) are required");
   }
   Carve cv(dry ? nullptr : a->workspace);
   const bool need_gc = a->g_cumsum == nullptr;
@@ -267,6 +270,7 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
     hh = h;
   }
   if ((rc = simt::bwd_dh(s, a->q, gcc, a->do_, a->dht, dh, a->dh0, st))) return rc;
+  if (dh0_only) return TOPS_OK;
   const float* AA = a->A;
   if (need_A) {
     if ((rc = simt::fwd_intra(s, a->q, a->k, gcc, 1, A, st))) return rc;

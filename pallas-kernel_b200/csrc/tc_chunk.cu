@@ -1283,10 +1283,11 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   okm = okm && map_tok(&sm.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_state_store(&sm.st, sv.h, s.B * NTb * s.H, s.K, s.V);
   OutMaps om;
-  okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
-        map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) && map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64) &&
-        map_tok(&om.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  if (o != nullptr)
+    okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
+          map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) &&
+          map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   {
@@ -1300,6 +1301,7 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   }
   int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, "tc_scan");
   if (rc) return rc;
+  if (o == nullptr) return TOPS_OK;  // final state only
   {
     LaunchTimer lt(st, "tc_out");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 0, static_cast<bf16*>(o)};
@@ -1346,6 +1348,11 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   bool okm = map_tok(&sm.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
              map_tok(&sm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
              map_state_store(&sm.st, dhs, s.B * NTb * s.H, s.K, s.V);
+  const bool dh0_only = dq == nullptr;  // dq, dk, dv, dg all NULL: the reverse scan alone
+  if (dh0_only) {
+    if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
+    return run_scan(s, sm, 1, sv.D, dht, dh0, nullptr, sb, spn, st, "tc_scan_bwd");
+  }
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) && map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&

@@ -80,17 +80,19 @@ def suffix_grads(dh0_local: torch.Tensor, D: torch.Tensor, dht: torch.Tensor | N
     return torch.stack(out, 0)
 
 
-def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, h0=None, group=None):
+def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, h0=None, group=None,
+                         local_final: Callable | None = None):
     """Forward of one rank's span.
 
     local_fwd(q, k, v, g, h0) -> (o, final_state) runs the chunked forward on this span;
-    span_decay(g) -> D [N, H, K] is exp of the span's gate sums.  ``h0`` (rank 0's initial
-    state) is read on every rank (pass the same tensor or None).  Returns (o, H_in, ht_global)
-    where H_in is this rank's incoming state and ht_global the final state of the whole
-    sequence (identical on all ranks).
+    span_decay(g) -> D [N, H, K] is exp of the span's gate sums; local_final(q, k, v, g)
+    -> the span's final state from a zero state (default: local_fwd's).  ``h0`` (rank 0's
+    initial state) is read on every rank (pass the same tensor or None).  Returns
+    (o, H_in, ht_global) where H_in is this rank's incoming state and ht_global the final
+    state of the whole sequence (identical on all ranks).
     """
     rank = dist.get_rank(group)
-    _, S = local_fwd(q, k, v, g, None)
+    S = local_final(q, k, v, g) if local_final is not None else local_fwd(q, k, v, g, None)[1]
     D = span_decay(g)
     S_all = all_gather_stack(S, group)
     D_all = all_gather_stack(D.to(S.dtype), group)
@@ -101,16 +103,18 @@ def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, 
     return o, H_in, ht_global
 
 
-def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=None, group=None):
+def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=None, group=None,
+                          local_dh0: Callable | None = None):
     """Backward of one rank's span.
 
     local_bwd(H_in, do, dht) -> (dq, dk, dv, dg, dh0) runs the chunked backward of this span
-    from its incoming state.  D: this span's decay [N, H, K].  ``dht`` is the gradient of the
+    from its incoming state; local_dh0(H_in, do) -> dh0 of the span's own loss alone
+    (default: local_bwd's).  D: this span's decay [N, H, K].  ``dht`` is the gradient of the
     whole sequence's final state (read by the last rank).  Returns (dq, dk, dv, dg, dh0) where
     dh0 is the gradient w.r.t. this rank's incoming state (rank 0: the user's initial state).
     """
     rank = dist.get_rank(group)
-    *_, dh0_local = local_bwd(H_in, do, None)
+    dh0_local = local_dh0(H_in, do) if local_dh0 is not None else local_bwd(H_in, do, None)[-1]
     L_all = all_gather_stack(dh0_local, group)
     D_all = all_gather_stack(D.to(dh0_local.dtype), group)
     G_all = suffix_grads(L_all, D_all, dht)
@@ -123,13 +127,20 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
         from .ops.gla import _core
 
         p = _core.make_plan(q, v.shape[-1], chunk_size, None, scale)
+        saved = {}
 
         def local_fwd(q_, k_, v_, g_, h_):
-            o, ht, _ = _core.chunk_fwd(p, q_, k_, v_, g_, h_, True, save=False)
+            o, ht, sv = _core.chunk_fwd(p, q_, k_, v_, g_, h_, True, save=True)
+            saved.update(sv)
             return o, ht
 
-        o, H_in, ht = seq_parallel_forward(local_fwd, lambda g_: _core.span_decay(p, g_), q, k, v, g, h0, group)
+        def local_final(q_, k_, v_, g_):  # state scan only
+            return _core.final_state(p, q_, k_, v_, g_, None)
+
+        o, H_in, ht = seq_parallel_forward(local_fwd, lambda g_: _core.span_decay(p, g_), q, k, v, g, h0, group,
+                                           local_final=local_final)
         ctx.save_for_backward(q, k, v, g, H_in)
+        ctx.fwd_saved = saved
         ctx.plan, ctx.group, ctx.has_h0 = p, group, h0 is not None
         return o, ht
 
@@ -138,14 +149,19 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
         from .ops.gla import _core
 
         q, k, v, g, H_in = ctx.saved_tensors
-        p = ctx.plan
+        p, sv = ctx.plan, ctx.fwd_saved
 
         def local_bwd(h_in, do_, dht_):
-            return _core.chunk_bwd(p, q, k, v, g, h_in, do_, dht_, want_dh0=True)
+            return _core.chunk_bwd(p, q, k, v, g, h_in, do_, dht_, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
+                                   want_dh0=True, block=sv.get("block"))
+
+        def local_dh0(h_in, do_):  # reverse state scan only
+            return _core.initial_state_grad(p, q, k, v, g, h_in, do_, None, block=sv.get("block"))
 
         D = _core.span_decay(p, g)
         dq, dk, dv, dg, dh0 = seq_parallel_backward(local_bwd, D, H_in, do.contiguous().to(q.dtype),
-                                                    None if dht is None else dht.float(), ctx.group)
+                                                    None if dht is None else dht.float(), ctx.group,
+                                                    local_dh0=local_dh0)
         rank = dist.get_rank(ctx.group)
         d_h0 = dh0 if (ctx.has_h0 and rank == 0) else None
         return dq, dk, dv, dg, d_h0, None, None, None

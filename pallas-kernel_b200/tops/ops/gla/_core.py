@@ -139,6 +139,33 @@ def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh
     return dq, dk, dv, dg, dh0
 
 
+def final_state(p: Plan, q, k, v, g, h0):
+    """Final state only (the state scan without the output GEMM): the first pass of a
+    sequence-parallel forward.  -> [N, H, K, V] fp32."""
+    dev = q.device
+    ht = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev)
+    a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), None, _C.ptr(ht),
+                        None, None, None, None, 0, None, 0)
+    ws = _ws(_C.lib().tops_gla_chunk_fwd_workspace_size(a), dev)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_chunk_fwd", a, _C.stream_of(q))
+    return ht
+
+
+def initial_state_grad(p: Plan, q, k, v, g, h0, do, dht, block=None):
+    """dL/dh0 only (the reverse state scan): the first pass of a sequence-parallel
+    backward.  ``block`` is the forward's saved block when it ran on the tensor-core path."""
+    dev = q.device
+    dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev)
+    a = _C.ChunkBwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(do), _C.ptr(dht),
+                        None, None, None, None, None, None, None, _C.ptr(dh0), None, 0, _C.ptr(block),
+                        0 if block is None else block.numel())
+    ws = _ws(_C.lib().tops_gla_chunk_bwd_workspace_size(a), dev)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), (ws.numel() if ws is not None else 0)
+    _C.call("tops_gla_chunk_bwd", a, _C.stream_of(q))
+    return dh0
+
+
 # ---------------------------------------------------------------------------
 # sub-functions
 # ---------------------------------------------------------------------------

@@ -443,3 +443,28 @@ def test_tc_long_sequence_takes_the_span_split_scan(gla):
     names = {n for n, _ in _C.timing_collect()}
     assert {"tc_scan_span", "tc_span_prefix", "tc_scan", "tc_scan_bwd_span", "tc_scan_bwd"} <= names, names
     assert _C.lib().tops_gla_device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,K,V", [(torch.bfloat16, 128, 128), (torch.float32, 64, 96)],
+                         ids=["tensor-core", "cuda-core"])
+def test_state_only_modes_match_full_calls(gla, dtype, K, V):
+    """C ABI: o == NULL gives the forward's final state alone; all-NULL gradients give dh0 alone."""
+    from tops import _C
+    from tops.ops.gla import _core
+    torch.manual_seed(3)
+    B, T, H = 2, 700, 2
+    q, k = (torch.randn(B, T, H, K, device="cuda").to(dtype) for _ in range(2))
+    v = torch.randn(B, T, H, V, device="cuda").to(dtype)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device="cuda")) / 16).contiguous()
+    h0 = torch.randn(B, H, K, V, device="cuda")
+    do = torch.randn(B, T, H, V, device="cuda").to(dtype)
+    p = _core.make_plan(q, V, 64, None, K ** -0.5)
+    o, ht, sv = _core.chunk_fwd(p, q, k, v, g, h0, True, save=True)
+    ht_only = _core.final_state(p, q, k, v, g, h0)
+    torch.testing.assert_close(ht_only, ht, rtol=1e-5, atol=1e-5)
+    full = _core.chunk_bwd(p, q, k, v, g, h0, do, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
+                           want_dh0=True, block=sv.get("block"))
+    dh0 = _core.initial_state_grad(p, q, k, v, g, h0, do, None, block=sv.get("block"))
+    torch.testing.assert_close(dh0, full[4], rtol=1e-5, atol=1e-5)
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
