@@ -6,7 +6,9 @@ GLA-1.3B layer shape B=8, T=4096, H=4, K=256, V=512, chunk 64, bf16 q/k/v/do,
 fp32 gates g = logsigmoid(N(0,1))/16, h0 = 0.  One step = fwd (saving what the
 backward needs) + bwd -> dq, dk, dv, dg.  Metric: tokens/s (B*T per step, summed
 over ranks).  The same line carries the decode step (
-fused_recurrent_gla, B=256, T=1, H=16, K=V=128, fp32 state) in HBM GB/s.
+fused_recurrent_gla, B=256, T=1, H=16, K=V=128, fp32 state) in HBM GB/s, and the
+long-context step (one sequence of T=131072, H=16, K=V=128; on
+N GPUs each rank holds T/N tokens and the span states are exchanged over NCCL).
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 batch x heads shard -- the units are independent, so there is no collective on
@@ -36,6 +38,7 @@ sys.path.insert(0, str(ROOT / "pallas-kernel_b200"))
 METRIC = "chunk_gla fwd+bwd tokens/s (1-8 B200), % tensor peak; decode step HBM GB/s"
 CFG3 = dict(B=8, T=4096, H=4, K=256, V=512, C=64)
 CFG2 = dict(B=256, T=1, H=16, K=128, V=128)
+CFG4 = dict(B=1, T=131072, H=16, K=128, V=128, C=64)
 
 
 def peaks():
@@ -364,6 +367,9 @@ def run_ours(args):
     # ---- decode step (config 2) -------------------------------------------------
     dec = decode_bench(args, world, local, dev)
 
+    # ---- long context (config 4) ---------------------------------------------------
+    lc = long_context_bench(args, world, rank, local, dev)
+
     # ---- end to end through the public API with host buffers ---------------------
     e2e = e2e_bench(args, world, dev, q, k, v, g, do, plan)
     clk.__exit__()
@@ -378,7 +384,7 @@ def run_ours(args):
                            "K": K, "V": V, "chunk_size": C, "global_batch": B * world,
                            "parallelism": f"batch x heads shards, {world} GPU(s), no collective",
                            "l2": "inputs (537 MB/step) larger than L2; no flush"},
-                "roofline": roof, "step_roofline": step_roof, "decode": dec, "e2e": e2e,
+                "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc, "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -424,6 +430,62 @@ def decode_bench(args, world, local, dev):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"], "kernel": "recurrent_fwd"},
             "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "state": "fp32", "inputs": "bf16 q/k/v, fp32 gk"}}
+
+
+def long_context_bench(args, world, rank, local, dev):
+    """Config 4: chunk_gla fwd+bwd over one long sequence.  1 GPU: the whole sequence (state
+    scans split into parallel spans).  N GPUs: rank r holds tokens [r T/N, (r+1) T/N); the
+    forward runs a state-only pass, all-gathers (final state, span decay) and re-runs from its
+    incoming state; the backward does the same with dh0 (tops.distributed, NCCL)."""
+    import torch
+
+    from tops.ops.gla import _core
+    c = CFG4
+    B, T, H, K, V, C = c["B"], c["T"], c["H"], c["K"], c["V"], c["C"]
+    Tr = T // world
+    gen = torch.Generator(device=dev).manual_seed(21 + rank)
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, Tr, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
+    v = torch.randn(B, Tr, H, V, device=dev, generator=gen).to(bf)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, Tr, H, K, device=dev, generator=gen)) / 16).contiguous()
+    do = torch.randn(B, Tr, H, V, device=dev, generator=gen).to(bf)
+    plan = _core.make_plan(q, V, C, None, K ** -0.5)
+
+    if world == 1:
+        def step():
+            o, _, sv = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+            return _core.chunk_bwd(plan, q, k, v, g, None, do, None, block=sv.get("block"))
+    else:
+        from tops import distributed as TD
+
+        def step():
+            S = _core.final_state(plan, q, k, v, g, None)
+            D = _core.span_decay(plan, g)
+            S_all, D_all = TD.all_gather_stack(S), TD.all_gather_stack(D)
+            H_in = TD.prefix_states(S_all, D_all, None)[rank]
+            o, _, sv = _core.chunk_fwd(plan, q, k, v, g, H_in, False, save=True)
+            L = _core.initial_state_grad(plan, q, k, v, g, H_in, do, None, block=sv.get("block"))
+            G = TD.suffix_grads(TD.all_gather_stack(L), D_all, None)[rank]
+            return _core.chunk_bwd(plan, q, k, v, g, H_in, do, G, want_dh0=True, block=sv.get("block"))
+
+    for _ in range(3):
+        step()
+    steps = max(3, min(args.steps, 5))
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    del q, k, v, g, do
+    return {"metric": "chunk_gla fwd+bwd tokens/s, long context (BASELINE config 4)", "value": B * T / (ms * 1e-3),
+            "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
+            "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "T_per_gpu": Tr,
+                       "parallelism": "1 GPU (state scans in parallel spans)" if world == 1 else
+                       f"sequence spans over {world} GPUs, all-gather of span states and dh0 (NCCL)"}}
 
 
 def e2e_bench(args, world, dev, q, k, v, g, do, plan):

@@ -468,3 +468,22 @@ def test_state_only_modes_match_full_calls(gla, dtype, K, V):
     torch.testing.assert_close(dh0, full[4], rtol=1e-5, atol=1e-5)
     torch.cuda.synchronize()
     assert _C.lib().tops_gla_device_error() == 0
+
+
+@pytest.mark.parametrize("T,cu", [(5000, None), (3001, [0, 17, 1500, 3001])], ids=["fixed", "varlen"])
+def test_span_decay_matches_torch(gla, T, cu):
+    """exp(sum of a span's gates) per (sequence, head, K column): the sequence-parallel decay."""
+    from tops.ops.gla import _core
+    torch.manual_seed(1)
+    B = 2 if cu is None else 1
+    H, K = 3, 96
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device="cuda")) / 16).contiguous()
+    q = torch.zeros(B, T, H, K, device="cuda")
+    cut = None if cu is None else torch.tensor(cu, dtype=torch.int32, device="cuda")
+    p = _core.make_plan(q, 32, 64, cut, 1.0)
+    got = _core.span_decay(p, g)
+    if cu is None:
+        want = torch.exp(g.double().sum(1))
+    else:
+        want = torch.stack([torch.exp(g[0, a:b].double().sum(0)) for a, b in zip(cu, cu[1:])])
+    torch.testing.assert_close(got.double(), want, rtol=1e-5, atol=1e-6)
