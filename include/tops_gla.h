@@ -260,6 +260,31 @@ TOPS_API int tops_gla_span_decay(const tops_gla_shape* s, const float* g, float*
 TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, const float* decay, const float* h_in,
                            const float* s_local, float* out, void* stream);
 
+/* ---- GLA layer pieces around the chunked op ------------ */
+
+/* Fused RMSNorm x swish output gate over rows of V: y = x * rstd * w * silu(g),
+ * rstd = 1/sqrt(mean(x^2) + eps) (written to rstd[rows], fp32, for the backward).
+ * x, g, w, y in `dtype` (TOPS_F32 or TOPS_BF16); w may be NULL (no affine weight).
+ * Replaces FusedRMSNormGated (tops/modules/fused_norm_gate.py:28; gold
+ * tests/src/modules/fused_norm_gate.py:30-44) used by tops/layers/gla.py:323-329.
+ * V: a multiple of 16 bytes, at most 512 (fp32) / 1024 (bf16) elements. */
+TOPS_API int tops_gla_norm_gate_fwd(int64_t rows, int32_t V, int32_t dtype, float eps, const void* x, const void* g,
+                                    const void* w, void* y, float* rstd, void* stream);
+/* Backward: dx, dg (dtype) and, when dw != NULL, dw[V] (dtype, deterministic sum over
+ * rows through the workspace). */
+TOPS_API size_t tops_gla_norm_gate_bwd_workspace_size(int64_t rows, int32_t V);
+TOPS_API int tops_gla_norm_gate_bwd(int64_t rows, int32_t V, int32_t dtype, const void* dy, const void* x,
+                                    const void* g, const void* w, const float* rstd, void* dx, void* dg, void* dw,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gate activation gk = logsigmoid(x) / normalizer, max(gk, clamp_min) when has_clamp;
+ * x in dtype, gk fp32 (tops/layers/gla.py:285-287).  Backward: dx = dgk * sigmoid(-x) /
+ * normalizer (0 where clamped). */
+TOPS_API int tops_gla_gate_logsigmoid_fwd(int64_t n, int32_t dtype, float normalizer, float clamp_min,
+                                          int32_t has_clamp, const void* x, float* out, void* stream);
+TOPS_API int tops_gla_gate_logsigmoid_bwd(int64_t n, int32_t dtype, float normalizer, float clamp_min,
+                                          int32_t has_clamp, const void* x, const float* dy, void* dx, void* stream);
+
 /* ---- XLA custom calls (JAX frontend) ---------------------------------------
  * Status-returning legacy custom-call signature used by jax custom_call lowering:
  * (cudaStream_t, void** buffers, const char* opaque, size_t opaque_len,

@@ -100,6 +100,12 @@ SIGNATURES = {
                                           VP]),
     "tops_gla_span_decay": (C.c_int, [C.POINTER(Shape), VP, VP, VP]),
     "tops_gla_state_combine": (C.c_int, [I32, I32, I32, I32, VP, VP, VP, VP, VP]),
+    "tops_gla_norm_gate_fwd": (C.c_int, [C.c_int64, I32, I32, F32C, VP, VP, VP, VP, VP, VP]),
+    "tops_gla_norm_gate_bwd_workspace_size": (C.c_size_t, [C.c_int64, I32]),
+    "tops_gla_norm_gate_bwd": (C.c_int, [C.c_int64, I32, I32, VP, VP, VP, VP, VP, VP, VP, VP, VP, C.c_size_t,
+                                         VP]),
+    "tops_gla_gate_logsigmoid_fwd": (C.c_int, [C.c_int64, I32, F32C, F32C, I32, VP, VP, VP]),
+    "tops_gla_gate_logsigmoid_bwd": (C.c_int, [C.c_int64, I32, F32C, F32C, I32, VP, VP, VP, VP]),
     "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
