@@ -8,7 +8,10 @@ backward needs) + bwd -> dq, dk, dv, dg.  Metric: tokens/s (B*T per step, summed
 over ranks).  The same line carries the decode step (
 fused_recurrent_gla, B=256, T=1, H=16, K=V=128, fp32 state) in HBM GB/s, and the
 long-context step (one sequence of T=131072, H=16, K=V=128; on
-N GPUs each rank holds T/N tokens and the span states are exchanged over NCCL).
+N GPUs each rank holds T/N tokens and the span states are exchanged over NCCL) and a
+training step of the config-5 model (24 GLA layers + SwiGLU, hidden 2048, vocab 32000,
+global batch 16 x 2048 tokens, bf16 weights with fp32-master AdamW, data parallel over
+NCCL at N>1).
 
 Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
 batch x heads shard -- the units are independent, so there is no collective on
@@ -370,6 +373,11 @@ def run_ours(args):
     # ---- long context (config 4) ---------------------------------------------------
     lc = long_context_bench(args, world, rank, local, dev)
 
+    # ---- config-5 model training step (GLA layers + SwiGLU, data parallel) -----------
+    torch.cuda.empty_cache()
+    lm = None if args.no_model else model_bench(args, world, rank, local, dev)
+    torch.cuda.empty_cache()
+
     # ---- end to end through the public API with host buffers ---------------------
     e2e = e2e_bench(args, world, dev, q, k, v, g, do, plan)
     clk.__exit__()
@@ -384,7 +392,8 @@ def run_ours(args):
                            "K": K, "V": V, "chunk_size": C, "global_batch": B * world,
                            "parallelism": f"batch x heads shards, {world} GPU(s), no collective",
                            "l2": "inputs (537 MB/step) larger than L2; no flush"},
-                "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc, "e2e": e2e,
+                "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc, "model_dp": lm,
+                "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -488,6 +497,54 @@ def long_context_bench(args, world, rank, local, dev):
                        f"sequence spans over {world} GPUs, all-gather of span states and dh0 (NCCL)"}}
 
 
+def model_bench(args, world, rank, local, dev):
+    """Config 5: one training step (forward, next-token loss, backward, gradient all-reduce
+    when N>1, fp32-master AdamW) of the 24-layer GLA + SwiGLU model on synthetic tokens
+    U[0, vocab); global batch 16 x 2048 split over the ranks."""
+    import torch
+
+    import tops.layers as L
+    cfg = L.GLAConfig()
+    B, T = max(1, 16 // world), 2048
+    with torch.device(dev):
+        model = L.GLAForCausalLM(cfg)
+    model.reset_parameters(torch.Generator(device=dev).manual_seed(5))
+    model = model.to(torch.bfloat16)
+    n_params = sum(p.numel() for p in model.parameters())
+    opt = L.MasterAdamW(model.parameters())
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=100)
+    gen = torch.Generator(device=dev).manual_seed(31 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, T), device=dev, generator=gen)
+    for _ in range(2):
+        L.train_step(net, opt, ids)
+    steps = max(2, min(args.steps, 3))
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        loss = L.train_step(net, opt, ids)
+    e1.record(s)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    tokens = B * T * world
+    K, V, H = int(cfg.hidden_size * cfg.expand_k) // cfg.num_heads, int(cfg.hidden_size * cfg.expand_v) // cfg.num_heads, cfg.num_heads
+    flops = 6 * n_params * tokens + cfg.num_layers * fwd_bwd_flops_per_token_head(K, V, 64) * H * tokens
+    pk = peaks()
+    out = {"metric": "GLA LM training tokens/s (BASELINE config 5)", "value": tokens / (ms * 1e-3), "unit": "tokens/s",
+           "ms_per_step": ms, "steps": steps, "scaling": "strong", "loss": float(loss),
+           "params": n_params, "model_tflops": flops / (ms * 1e-3) / 1e12,
+           "tensor_frac": flops / (ms * 1e-3) / 1e12 / pk["bf16_sustained"],
+           "config": {"layers": cfg.num_layers, "hidden": cfg.hidden_size, "heads": H, "K": K, "V": V,
+                      "mlp": cfg.intermediate_size, "vocab": cfg.vocab_size, "global_batch": B * world, "T": T,
+                      "dtype": "bf16 weights/activations, fp32 master AdamW",
+                      "parallelism": "1 GPU" if world == 1 else f"data parallel x{world} (DDP all-reduce, NCCL)"}}
+    del net, model, opt, ids
+    return out
+
+
 def e2e_bench(args, world, dev, q, k, v, g, do, plan):
     """Public C-ABI path with HOST buffers: H2D of q,k,v,g,do and D2H of dq,dk,dv,dg per step."""
     import torch
@@ -531,6 +588,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (profiling runs on a smaller case)")
+    ap.add_argument("--no-model", action="store_true", help="skip the config-5 model training leg")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the timed fwd+bwd loop (no decode / e2e / CPU legs); for ncu launch lists")
     args = ap.parse_args()
