@@ -123,12 +123,17 @@ def chunk_fwd(p: Plan, q, k, v, g, h0, output_final_state: bool, save: bool):
     return o, ht, ({"block": blk} if blk is not None else {"g_cumsum": gc, "A": A, "h": h})
 
 
-def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh0: bool = False, block=None):
+def chunk_bwd(p: Plan, q, k, v, g, h0, do, dht, gc=None, A=None, h=None, want_dh0: bool = False, block=None,
+              out=None):
+    """-> dq, dk, dv, dg, dh0|None; ``out`` = preallocated (dq, dk, dv, dg) to write into."""
     dev = q.device
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
-    dg = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
+    if out is not None:
+        dq, dk, dv, dg = out
+    else:
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        dg = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
     dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_dh0 else None
     a = _C.ChunkBwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h0), _C.ptr(do), _C.ptr(dht),
                         _C.ptr(gc), _C.ptr(A), _C.ptr(h), _C.ptr(dq), _C.ptr(dk), _C.ptr(dv), _C.ptr(dg),

@@ -487,3 +487,26 @@ def test_span_decay_matches_torch(gla, T, cu):
     else:
         want = torch.stack([torch.exp(g[0, a:b].double().sum(0)) for a, b in zip(cu, cu[1:])])
     torch.testing.assert_close(got.double(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_pinned_host_fwd_bwd_matches_device_calls(gla):
+    """chunk_gla_fwd_bwd_pinned (host tensors, sliced over the batch, three streams) gives
+    the gradients of the device-side forward + backward."""
+    from tops.ops.gla import _core
+    torch.manual_seed(9)
+    B, T, H, K, V = 3, 520, 2, 128, 256
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, T, H, K).to(bf).pin_memory() for _ in range(2))
+    v = torch.randn(B, T, H, V).to(bf).pin_memory()
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K)) / 16).pin_memory()
+    do = torch.randn(B, T, H, V).to(bf).pin_memory()
+    got = gla.chunk_gla_fwd_bwd_pinned(q, k, v, g, do, chunk_size=64, slice_batch=1, depth=2)
+    torch.cuda.synchronize()
+    qd, kd, vd, gd, dod = (x.cuda() for x in (q, k, v, g, do))
+    p = _core.make_plan(qd, V, 64, None, K ** -0.5)
+    o, _, sv = _core.chunk_fwd(p, qd, kd, vd, gd, None, False, save=True)
+    want = _core.chunk_bwd(p, qd, kd, vd, gd, None, dod, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"), False,
+                           block=sv.get("block"))
+    for nm, a, b in zip(("dq", "dk", "dv", "dg"), got, want[:4]):
+        assert not a.is_cuda and a.is_pinned()
+        assert_rel_l2(nm, a.float(), b.float().cpu(), 1e-3)
