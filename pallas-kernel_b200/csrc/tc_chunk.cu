@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
   unsigned char* qt = gb + 2 * TILE_BYTES;    // q e^{G-Gm}
   unsigned char* kt = qt + TILE_BYTES;        // k e^{Gm-G}
   __shared__ __align__(16) float wtot[8][64];  // per-warp column sums of g
-  __shared__ __align__(8) uint64_t bar_load, bar_mma;
+  __shared__ __align__(8) uint64_t bar_g, bar_qk, bar_mma;
   __shared__ uint32_t tmem_base;
 
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -150,9 +150,15 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
     ptx::tmem_relinquish();
   }
   if (tid == 0) {
-    ptx::mbar_init(&bar_load, 1);
+    ptx::mbar_init(&bar_g, 1);
+    ptx::mbar_init(&bar_qk, 1);
     ptx::mbar_init(&bar_mma, 1);
     ptx::fence_mbar_init();
+    // the gates of K block 0; each later block's gates load as soon as the previous
+    // block's gates are in registers (g tiles free), ahead of its q / k tiles
+    ptx::mbar_arrive_expect_tx(&bar_g, 2 * TILE_BYTES);
+    ptx::tma_load_4d(gb, &maps.g, 0, h, row0, b, &bar_g);
+    ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, 32, h, row0, b, &bar_g);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -169,19 +175,15 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
   for (int kbi = 0; kbi < nkb && ok; ++kbi) {
     if (tid == 0) {
       if (kbi > 0) ptx::bulk_wait_read<0>();  // previous qhat/kdec stores have read qb/kb
-      ptx::mbar_arrive_expect_tx(&bar_load, 4 * TILE_BYTES);
-      ptx::tma_load_4d(qb, &maps.q, kbi * 64, h, row0, b, &bar_load);
-      ptx::tma_load_4d(kb, &maps.k, kbi * 64, h, row0, b, &bar_load);
-      ptx::tma_load_4d(gb, &maps.g, kbi * 64, h, row0, b, &bar_load);
-      ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, kbi * 64 + 32, h, row0, b, &bar_load);
-      if (kbi + 1 < nkb) {  // the next K block into L2 while this one is gated
+      ptx::mbar_arrive_expect_tx(&bar_qk, 2 * TILE_BYTES);
+      ptx::tma_load_4d(qb, &maps.q, kbi * 64, h, row0, b, &bar_qk);
+      ptx::tma_load_4d(kb, &maps.k, kbi * 64, h, row0, b, &bar_qk);
+      if (kbi + 1 < nkb) {  // the next K block's q, k into L2 while this one is gated
         ptx::tma_prefetch_4d(&maps.q, kbi * 64 + 64, h, row0, b);
         ptx::tma_prefetch_4d(&maps.k, kbi * 64 + 64, h, row0, b);
-        ptx::tma_prefetch_4d(&maps.g, kbi * 64 + 64, h, row0, b);
-        ptx::tma_prefetch_4d(&maps.g, kbi * 64 + 96, h, row0, b);
       }
     }
-    ok = ptx::mbar_wait(&bar_load, (uint32_t)(kbi & 1));
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_g, (uint32_t)(kbi & 1)));  // uniform exit on a timeout
     if (!ok) break;
     const unsigned char* gt = gb + (c8 >> 2) * TILE_BYTES;
     float gv[4][8], ps[8];
@@ -208,7 +210,13 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       ps[j] = v - own;  // sum of this warp's rows above this quad
       if (sub == 3) wtot[warp][c8 * 8 + j] = v;
     }
-    __syncthreads();
+    __syncthreads();  // every thread holds its gates: the g tiles are free
+    if (tid == 0 && kbi + 1 < nkb) {
+      ptx::fence_async_smem();
+      ptx::mbar_arrive_expect_tx(&bar_g, 2 * TILE_BYTES);
+      ptx::tma_load_4d(gb, &maps.g, kbi * 64 + 64, h, row0, b, &bar_g);
+      ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, kbi * 64 + 96, h, row0, b, &bar_g);
+    }
     float off[8], gm[8], gl[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -239,16 +247,25 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       reinterpret_cast<float4*>(dp)[0] = make_float4(__expf(gl[0]), __expf(gl[1]), __expf(gl[2]), __expf(gl[3]));
       reinterpret_cast<float4*>(dp)[1] = make_float4(__expf(gl[4]), __expf(gl[5]), __expf(gl[6]), __expf(gl[7]));
     }
-    float run[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) run[j] = off[j] - gm[j];  // running G - Gm
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_qk, (uint32_t)(kbi & 1)));
+    if (!ok) break;
+    // all loads of the four rows first, then the arithmetic, then the stores (the
+    // compiler cannot move loads across stores to buffers it cannot disambiguate)
+    uint4 xq[4], xk[4];
 #pragma unroll
     for (int rr = 0; rr < 4; ++rr) {
       const uint32_t o = ptx::sw128(r0 + rr, c8 * 16);
-      uint4 xq = *reinterpret_cast<const uint4*>(qb + o), xk = *reinterpret_cast<const uint4*>(kb + o);
-      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&xq);
-      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&xk);
-      uint32_t wqt[4], wkt[4], wqh[4], wkd[4];
+      xq[rr] = *reinterpret_cast<const uint4*>(qb + o);
+      xk[rr] = *reinterpret_cast<const uint4*>(kb + o);
+    }
+    float run[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) run[j] = off[j] - gm[j];  // running G - Gm
+    uint32_t wqt[4][4], wkt[4][4], wqh[4][4], wkd[4][4];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&xq[rr]);
+      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&xk[rr]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 fq = __bfloat1622float2(q2[e]), fk = __bfloat1622float2(k2[e]);
@@ -257,15 +274,19 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
         const float a0 = __expf(run[2 * e]), a1 = __expf(run[2 * e + 1]);
         const float b0 = __expf(-run[2 * e]), b1 = __expf(-run[2 * e + 1]);
         const float qt0 = fq.x * a0, qt1 = fq.y * a1, kt0 = fk.x * b0, kt1 = fk.y * b1;
-        wqt[e] = ptx::pack_bf16(qt0, qt1);
-        wkt[e] = ptx::pack_bf16(kt0, kt1);
-        wqh[e] = ptx::pack_bf16(qt0 * sq[2 * e], qt1 * sq[2 * e + 1]);
-        wkd[e] = ptx::pack_bf16(kt0 * sk[2 * e], kt1 * sk[2 * e + 1]);
+        wqt[rr][e] = ptx::pack_bf16(qt0, qt1);
+        wkt[rr][e] = ptx::pack_bf16(kt0, kt1);
+        wqh[rr][e] = ptx::pack_bf16(qt0 * sq[2 * e], qt1 * sq[2 * e + 1]);
+        wkd[rr][e] = ptx::pack_bf16(kt0 * sk[2 * e], kt1 * sk[2 * e + 1]);
       }
-      *reinterpret_cast<uint4*>(qt + o) = make_uint4(wqt[0], wqt[1], wqt[2], wqt[3]);
-      *reinterpret_cast<uint4*>(kt + o) = make_uint4(wkt[0], wkt[1], wkt[2], wkt[3]);
-      *reinterpret_cast<uint4*>(qb + o) = make_uint4(wqh[0], wqh[1], wqh[2], wqh[3]);
-      *reinterpret_cast<uint4*>(kb + o) = make_uint4(wkd[0], wkd[1], wkd[2], wkd[3]);
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const uint32_t o = ptx::sw128(r0 + rr, c8 * 16);
+      *reinterpret_cast<uint4*>(qt + o) = make_uint4(wqt[rr][0], wqt[rr][1], wqt[rr][2], wqt[rr][3]);
+      *reinterpret_cast<uint4*>(kt + o) = make_uint4(wkt[rr][0], wkt[rr][1], wkt[rr][2], wkt[rr][3]);
+      *reinterpret_cast<uint4*>(qb + o) = make_uint4(wqh[rr][0], wqh[rr][1], wqh[rr][2], wqh[rr][3]);
+      *reinterpret_cast<uint4*>(kb + o) = make_uint4(wkd[rr][0], wkd[rr][1], wkd[rr][2], wkd[rr][3]);
     }
     ptx::fence_async_smem();
     ptx::tc_fence_before();
@@ -280,7 +301,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       ptx::tma_store_4d(&maps.kd, kbi * 64, h, row0, b, kb);
       ptx::bulk_commit();
     }
-    ok = ptx::mbar_wait(&bar_mma, (uint32_t)(kbi & 1));
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_mma, (uint32_t)(kbi & 1)));
     ptx::tc_fence_after();
   }
   if (ok) {
@@ -314,6 +335,10 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       ptx::tma_store_4d(&maps.A, 64, h, row0, b, kt);
       ptx::bulk_commit();
     }
+  }
+  if (!ok && tid == 0) {  // drain loads that may still be in flight (bounded)
+    ptx::mbar_wait(&bar_g, 0);
+    ptx::mbar_wait(&bar_qk, 0);
   }
   if (tid == 0) ptx::bulk_wait<0>();
   ptx::tc_fence_before();
