@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
       issue(j + AHEAD);
       next_issue = j + AHEAD + 1;
     }
-    ok = ptx::mbar_wait(&bars[s], (uint32_t)((j / STAGES) & 1));
+    ok = ptx::bar_and(1, THREADS, ptx::mbar_wait(&bars[s], (uint32_t)((j / STAGES) & 1)));  // uniform exit
     if (!ok) {
       failed_at = j;
       break;

@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     dprod *= d;
     d_next = decay_of(i + 1);
     if (i > 0) {
-      ok = ptx::mbar_wait(&bar_mma, (uint32_t)((i - 1) & 1));
+      ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_mma, (uint32_t)((i - 1) & 1)));  // uniform exit on a timeout
       ptx::tc_fence_after();
       if (!ok) break;
       if (tid == 0 && i + 1 < n_it) issue(i + 1);  // buffer (i+1)&1 was read by chunk i-1, now complete
