@@ -6,10 +6,11 @@
 // (sequence, head) state is a contiguous K*V*4-byte tile, split into P row blocks
 // ("parts") of 32 KB.  A persistent CTA per SM streams its parts through a 6-stage
 // shared-memory ring: one thread issues 1D bulk copies (TMA) of the state part and
-// of the part's q/k/gk rows and v/gv vectors onto the stage's mbarrier; all threads
-// update the part in place in shared memory and accumulate o; a bulk store writes
-// the part back to ht.  Loads of the next parts and the stores of earlier ones stay
-// in flight while a part is updated, so HBM sees continuous read and write streams.
+// of the part's q/k/gk rows and v/gv vectors onto the stage's mbarrier; every thread
+// updates 16-byte column groups of the part's rows in registers, accumulates o, and
+// writes the new state straight to ht with coalesced 16-byte stores (a warp writes whole
+// 512-byte rows).  A stage is free as soon as it has been read, so five parts' loads
+// stay in flight while one is updated and HBM sees continuous read and write streams.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -18,7 +19,7 @@ namespace decode {
 
 constexpr int THREADS = 256;
 constexpr int STAGES = 6;
-constexpr int AHEAD = 4;  // loads issued ahead; leaves STAGES-AHEAD-1 stores free to drain
+constexpr int AHEAD = STAGES - 1;  // loads in flight while one stage is updated
 constexpr int PART_BYTES = 32 * 1024;
 constexpr int COEF_BYTES = 4 * 1024;  // q,k,gk rows + v,gv of one part (fits K_part,V <= 256)
 
@@ -42,15 +43,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
   const uint32_t off_k = qb, off_gk = 2 * qb, off_v = off_gk + (GK ? gkb : 0), off_gv = off_v + vb;
   const uint32_t coef_bytes = off_gv + (GV ? gvb : 0);
   __shared__ __align__(8) uint64_t bars[STAGES];
-  __shared__ float red[THREADS];
-  __shared__ float dks[256];  // e^{gk} of the part's rows (R <= 256)
+  __shared__ __align__(16) float red[THREADS * 4];
 
   auto stage_state = [&](int s) { return reinterpret_cast<float*>(smem + (size_t)s * (PART_BYTES + COEF_BYTES)); };
   auto stage_coef = [&](int s) { return smem + (size_t)s * (PART_BYTES + COEF_BYTES) + PART_BYTES; };
 
   const int tid = threadIdx.x;
-  const int G = THREADS / V;  // row groups (V divides THREADS)
-  const int col = tid % V, grp = tid / V;
+  const int VC = V / 4;        // 16-byte column groups per row
+  const int G = THREADS / VC;  // row groups (VC divides THREADS, G divides R)
+  const int c4 = tid % VC, grp = tid / VC;
   const int ntiles = (p.NH - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   const int nitems = ntiles * P;
   if (tid == 0) {
@@ -79,15 +80,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
 
   bool ok = true;
   int failed_at = nitems;
-  float acc = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < nitems; ++j) {
     const int s = j % STAGES;
     const int nh = (int)blockIdx.x + (j / P) * (int)gridDim.x, part = j % P;
     if (tid == 0 && j + AHEAD < nitems) {
-      // the stage for item j+AHEAD was last used by item j+AHEAD-STAGES; the stores of the
-      // STAGES-AHEAD-1 items after it may still be draining
-      if (HAS_HT) ptx::bulk_wait_read<STAGES - AHEAD - 1>();
-      issue(j + AHEAD);
+      issue(j + AHEAD);  // its stage was read by item j-1 (barrier at the end of the last iteration)
       next_issue = j + AHEAD + 1;
     }
     ok = ptx::bar_and(1, THREADS, ptx::mbar_wait(&bars[s], (uint32_t)((j / STAGES) & 1)));  // uniform exit
@@ -95,42 +93,45 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
       failed_at = j;
       break;
     }
-    float* buf = stage_state(s);
+    const float* buf = stage_state(s);
     const unsigned char* cf = stage_coef(s);
     const T* qs = reinterpret_cast<const T*>(cf);
     const T* ks = reinterpret_cast<const T*>(cf + off_k);
     const float* gks = reinterpret_cast<const float*>(cf + off_gk);
     const T* vs = reinterpret_cast<const T*>(cf + off_v);
     const float* gvs = reinterpret_cast<const float*>(cf + off_gv);
-    const float vc = to_f(vs[col]);
-    const float ec = GV ? expf(gvs[col]) : 1.f;
-    if (GK) {
-      for (int r = tid; r < R; r += THREADS) dks[r] = expf(gks[r]);
-      __syncthreads();
+    float vc[4], ec[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      vc[e] = to_f(vs[4 * c4 + e]);
+      ec[e] = GV ? expf(gvs[4 * c4 + e]) : 1.f;
     }
+    float* hrow = HAS_HT ? p.ht + ((size_t)nh * K + (size_t)part * R) * V + 4 * c4 : nullptr;
 #pragma unroll 4
     for (int r = grp; r < R; r += G) {
-      float x = HAS_H0 ? buf[r * V + col] : 0.f;
-      const float d = GK ? dks[r] : 1.f;
-      x = fmaf(to_f(ks[r]), vc, x * d * ec);
-      if (HAS_HT) buf[r * V + col] = x;
-      acc = fmaf(to_f(qs[r]), x, acc);
+      float4 x = HAS_H0 ? *reinterpret_cast<const float4*>(buf + r * V + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float d = GK ? expf(gks[r]) : 1.f;
+      const float kr = to_f(ks[r]), qr = to_f(qs[r]);
+      x.x = fmaf(kr, vc[0], x.x * d * ec[0]);
+      x.y = fmaf(kr, vc[1], x.y * d * ec[1]);
+      x.z = fmaf(kr, vc[2], x.z * d * ec[2]);
+      x.w = fmaf(kr, vc[3], x.w * d * ec[3]);
+      if (HAS_HT) *reinterpret_cast<float4*>(hrow + (size_t)r * V) = x;
+      acc.x = fmaf(qr, x.x, acc.x);
+      acc.y = fmaf(qr, x.y, acc.y);
+      acc.z = fmaf(qr, x.z, acc.z);
+      acc.w = fmaf(qr, x.w, acc.w);
     }
-    __syncthreads();  // all writes of this part done; coefficient reads done
-    if (HAS_HT && tid == 0) {
-      ptx::fence_async_smem();
-      ptx::bulk_store(p.ht + ((size_t)nh * K + (size_t)part * R) * V, buf, part_bytes);
-      ptx::bulk_commit();
-    }
+    __syncthreads();  // stage s has been read by every thread: it may be refilled
     if (part == P - 1) {
-      red[tid] = acc;
+      reinterpret_cast<float4*>(red)[grp * VC + c4] = acc;
       __syncthreads();
-      if (grp == 0) {
+      if (tid < V) {
         float o = 0.f;
-        for (int gi = 0; gi < G; ++gi) o += red[gi * V + col];
-        p.o[(size_t)nh * V + col] = o * p.scale;
+        for (int gi = 0; gi < G; ++gi) o += red[gi * V + tid];
+        p.o[(size_t)nh * V + tid] = o * p.scale;
       }
-      acc = 0.f;
+      acc = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncthreads();
     }
   }
@@ -139,7 +140,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
     for (int jj = failed_at + 1; jj < next_issue; ++jj)
       ptx::mbar_wait(&bars[jj % STAGES], (uint32_t)((jj / STAGES) & 1));
   }
-  if (HAS_HT && tid == 0) ptx::bulk_wait<0>();
   __syncthreads();
 }
 
@@ -158,6 +158,7 @@ bool supported(const tops_gla_recurrent_args& a) {
   if (!rows_per_part(a, R)) return false;
   const size_t es = a.dtype == TOPS_F32 ? 4 : 2;
   if ((R * es) % 16 != 0 || (a.V * es) % 16 != 0) return false;
+  if (R % (THREADS / (a.V / 4)) != 0) return false;  // row groups divide the part
   if (2 * R * es + 4 * R + a.V * es + 4 * a.V > (size_t)COEF_BYTES) return false;
   auto al = [](const void* x) { return x == nullptr || (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   return al(a.h0) && al(a.ht) && al(a.q) && al(a.k) && al(a.v) && al(a.gk) && al(a.gv);
