@@ -273,6 +273,14 @@ def run_ours(args):
 
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
+    if args.decode_only:
+        dec = decode_bench(args, world, local, dev)
+        if rank == 0:
+            print(json.dumps({"decode_only": True, **dec}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return 0
     c = CFG3
     B, T, H, K, V, C = c["B"], c["T"], c["H"], c["K"], c["V"], c["C"]
     q, k, v, g, do = make_inputs(dev, 1234 + rank)
@@ -586,6 +594,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch", type=int, default=None, help="override B per GPU (profiling runs on a smaller case)")
     ap.add_argument("--no-model", action="store_true", help="skip the config-5 model training leg")
+    ap.add_argument("--decode-only", action="store_true", help="only the config-2 decode leg (for ncu captures)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the timed fwd+bwd loop (no decode / e2e / CPU legs); for ncu launch lists")
     args = ap.parse_args()
