@@ -119,8 +119,9 @@ int read_device_error();
 namespace tc {
 bool eligible(const tops_gla_shape& s);
 size_t saved_bytes(const tops_gla_shape& s);
+size_t fwd_workspace(const tops_gla_shape& s, bool own_saved);
 int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
-        void* o, float* ht, void* saved, cudaStream_t st);
+        void* o, float* ht, void* saved, void* workspace, cudaStream_t st);
 int read_device_error();
 size_t bwd_workspace(const tops_gla_shape& s, bool have_saved);
 int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
@@ -162,15 +163,15 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
     const bool own = a->saved != nullptr;
     if (own && a->saved_bytes < need_saved)
       return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: saved block smaller than tops_gla_chunk_saved_size()");
+    const size_t need = tc::fwd_workspace(s, own);
     if (dry) {
-      *ws_need = own ? 0 : need_saved;
+      *ws_need = need;
       return TOPS_OK;
     }
     TOPS_CHECK_ARG(a->q && a->k && a->v && (a->o || a->ht), "chunk_fwd: q, k, v and o (or ht) are required");
-    void* blk = own ? a->saved : a->workspace;
-    if (!own && (a->workspace == nullptr || a->workspace_bytes < need_saved))
+    if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need))
       return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: workspace smaller than tops_gla_chunk_fwd_workspace_size()");
-    return tc::fwd(s, a->q, a->k, a->v, a->g, a->h0, a->o, a->ht, blk, S(stream));
+    return tc::fwd(s, a->q, a->k, a->v, a->g, a->h0, a->o, a->ht, own ? a->saved : nullptr, a->workspace, S(stream));
   }
   if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {

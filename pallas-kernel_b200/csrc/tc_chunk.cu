@@ -363,6 +363,9 @@ struct ScanParams {
   bf16* states;       // [B*NTb, H, K, V] bf16 (chunk-start states) or null
   int nspan, span_len, fin_mode;
   float* span_decay;  // [nspan][B, H, K] product of each span's chunk decays, or null
+  // segments of a padded varlen problem (B == 1, one span): sequence n owns blocks
+  // [blk_off[n], blk_off[n+1]); grid.z = sequences; init / fin indexed by sequence; or null
+  const int* blk_off;
 };
 
 struct ScanMaps {
@@ -385,10 +388,14 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   __shared__ __align__(8) uint64_t bar_full[2], bar_mma;
   __shared__ uint32_t tmem_base;
 
-  const int vt = blockIdx.x, h = blockIdx.y, b = blockIdx.z / p.nspan, sp_ = blockIdx.z % p.nspan;
+  const int vt = blockIdx.x, h = blockIdx.y;
+  const bool seg = p.blk_off != nullptr;
+  // b: batch index of the chunk data; sq: index of this CTA's initial / final state
+  const int b = seg ? 0 : blockIdx.z / p.nspan, sp_ = seg ? 0 : blockIdx.z % p.nspan;
+  const int sq = seg ? (int)blockIdx.z : b;
   const int v0 = vt * BV;
-  const int i0 = sp_ * p.span_len;                      // first iteration of this span
-  const int n_it = min(p.span_len, p.NTb - i0);         // iterations (chunks) of this span
+  const int i0 = seg ? p.blk_off[blockIdx.z] : sp_ * p.span_len;                        // first chunk
+  const int n_it = seg ? p.blk_off[blockIdx.z + 1] - i0 : min(p.span_len, p.NTb - i0);  // chunks
   const size_t span_off = (size_t)sp_ * p.B * p.H * p.K * p.V;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qd = warp & 3, hf = warp >> 2;  // lane quadrant, state half handled by this warp
@@ -414,7 +421,10 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   auto sbuf = [&](int i) { return tmem_base + (uint32_t)((i & 1) * 256); };
   constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, true, true);
 
-  auto chunk_of = [&](int i) { return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i; };
+  auto chunk_of = [&](int i) {
+    if (seg) return p.reverse ? i0 + n_it - 1 - i : i0 + i;
+    return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i;
+  };
   auto issue = [&](int i) {
     const int c = chunk_of(i);
     unsigned char* buf = smem + (i & 1) * buf_bytes;
@@ -424,12 +434,12 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     ptx::tma_load_4d(buf + (nkb + 1) * TILE_BYTES, &maps.y, v0 + 64, h, c * BT, b, &bar_full[i & 1]);
   };
   if (tid == 0) {
-    issue(0);
+    if (n_it > 0) issue(0);
     if (n_it > 1) issue(1);
   }
   // initial state -> TMEM buffer 0
   if (active) {
-    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0;
+    const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0;
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
@@ -522,12 +532,12 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     }
     // a failed wait in thread 0 leaves bar_mma pending: the next wait times out for everyone
   }
-  if (ok) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
+  if (ok && n_it > 0) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
   ptx::tc_fence_after();
   if (ok && active && p.span_decay && vt == 0)
     p.span_decay[((size_t)(sp_ * p.B + b) * p.H + h) * p.K + krow] = dprod;
   if (ok && active && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
-    const size_t srow = ((size_t)(b * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
+    const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
@@ -1212,9 +1222,90 @@ static size_t carve_spans(const tops_gla_shape& s, Spans spn, char* base, size_t
   return off;
 }
 
+// Varlen problems run on the fixed-length kernels after each segment is padded to a
+// multiple of BT rows and packed (the reference pads segments to its chunk size the same
+// way, tops/ops/gla/chunk.py:751-807): every BT-row block then lies inside one segment, and
+// only the state scans need the segment boundaries (blk_off).  The padded length is bounded
+// by (ceil(T/BT) + N) * BT rows, computed without reading cu_seqlens on the host.
+static int varlen_rows(const tops_gla_shape& s) { return ((s.T + BT - 1) / BT + s.N) * BT; }
+
+static tops_gla_shape padded_shape(const tops_gla_shape& s) {
+  tops_gla_shape p = s;
+  p.B = 1;
+  p.T = varlen_rows(s);
+  p.cu_seqlens = nullptr;
+  p.chunk_offsets = nullptr;
+  return p;
+}
+
 bool eligible(const tops_gla_shape& s) {
-  return s.dtype == TOPS_BF16 && s.cu_seqlens == nullptr && (s.K == 128 || s.K == 256) && s.V % BV == 0 &&
-         s.T > 0 && s.B > 0 && s.H > 0 && tops_gla_has_tcgen05() && encode_fn() != nullptr;
+  if (!(s.dtype == TOPS_BF16 && (s.K == 128 || s.K == 256) && s.V % BV == 0 && s.T > 0 && s.B > 0 && s.H > 0))
+    return false;
+  // packed varlen: only while the block padding at most doubles the rows (long segments)
+  if (s.cu_seqlens != nullptr && (s.B != 1 || s.N <= 0 || (size_t)varlen_rows(s) > 2 * (size_t)s.T + BT)) return false;
+  return tops_gla_has_tcgen05() && encode_fn() != nullptr;
+}
+
+__global__ void k_blk_off(const int32_t* __restrict__ cu, int N, int32_t* __restrict__ blk_off) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int acc = 0;
+    blk_off[0] = 0;
+    for (int n = 0; n < N; ++n) {
+      acc += (cu[n + 1] - cu[n] + BT - 1) / BT;
+      blk_off[n + 1] = acc;
+    }
+  }
+}
+
+// last n in [0, N) with a[n] <= x (a non-decreasing, a[0] <= x)
+__device__ __forceinline__ int seg_of(const int32_t* __restrict__ a, int N, int x) {
+  int lo = 0, hi = N - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// to_pad = 1: padded row r <- packed row (or zeros); to_pad = 0: packed row r <- padded row.
+// One warp per row, 16-byte vectors.
+__global__ void k_pad_rows(const uint4* __restrict__ src, uint4* __restrict__ dst, int row_vec, int rows,
+                           const int32_t* __restrict__ cu, const int32_t* __restrict__ blk_off, int N, int to_pad) {
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += gridDim.x * wpb) {
+    int other = -1;
+    if (to_pad) {
+      const int blk = r / BT;
+      if (blk < blk_off[N]) {
+        const int n = seg_of(blk_off, N, blk);
+        const int off = r - blk_off[n] * BT;
+        if (off < cu[n + 1] - cu[n]) other = cu[n] + off;
+      }
+    } else {
+      const int n = seg_of(cu, N, r);
+      other = blk_off[n] * BT + (r - cu[n]);
+    }
+    uint4* d = dst + (size_t)r * row_vec;
+    if (other >= 0) {
+      const uint4* sp = src + (size_t)other * row_vec;
+      for (int c = lane; c < row_vec; c += 32) d[c] = sp[c];
+    } else {
+      for (int c = lane; c < row_vec; c += 32) d[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+static int pad_rows(const void* src, void* dst, size_t row_bytes, int rows, const tops_gla_shape& s,
+                    const int32_t* blk_off, int to_pad, cudaStream_t st) {
+  if (rows <= 0) return TOPS_OK;
+  const int row_vec = (int)(row_bytes / 16);
+  int grid = (rows + 7) / 8;
+  if (grid > 148 * 16) grid = 148 * 16;
+  k_pad_rows<<<grid, 256, 0, st>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), row_vec, rows,
+                                   s.cu_seqlens, blk_off, s.N, to_pad);
+  TOPS_CUDA_LAUNCH_CHECK(to_pad ? "tc varlen pad" : "tc varlen unpad");
+  return TOPS_OK;
 }
 
 // Intermediates of the forward that the backward reuses (one contiguous block).
@@ -1224,7 +1315,7 @@ struct Saved {
   SpanBufs sb;  // scratch of a span-split forward scan (empty when the scan runs in one span)
 };
 
-static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
+static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv, bool spans = true) {
   const int NTb = (s.T + BT - 1) / BT;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1240,12 +1331,14 @@ static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv) {
   v.A = reinterpret_cast<bf16*>(take(tok * BT * 2));
   v.D = reinterpret_cast<float*>(take((size_t)s.B * NTb * s.H * s.K * 4));
   v.h = reinterpret_cast<bf16*>(take((size_t)s.B * NTb * s.H * s.K * s.V * 2));
-  off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb);
+  if (spans) off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb);
   if (sv) *sv = v;
   return off;
 }
 
-size_t saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nullptr); }
+size_t saved_bytes(const tops_gla_shape& s) {
+  return s.cu_seqlens ? carve_saved(padded_shape(s), nullptr, nullptr, false) : carve_saved(s, nullptr, nullptr);
+}
 
 static size_t prep_smem() { return 6 * TILE_BYTES + 1024; }
 static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 8 * 2 * 2048 + 1024; }
@@ -1258,20 +1351,28 @@ static cudaError_t set_smem(KernelT k, size_t bytes) {
 
 // One state scan (forward h or reverse dh), split into spans when that fills the GPU.
 static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, const float* D, const float* init,
-                    float* fin, bf16* states, const SpanBufs& sb, Spans spn, cudaStream_t st, const char* name) {
+                    float* fin, bf16* states, const SpanBufs& sb, Spans spn, cudaStream_t st, const char* name,
+                    const int* blk_off = nullptr) {
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  if (blk_off != nullptr) {  // padded varlen problem: one CTA column per segment
+    LaunchTimer lt(st, name);
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, blk_off};
+    k_scan<<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
+    TOPS_CUDA_LAUNCH_CHECK(name);
+    return TOPS_OK;
+  }
   if (spn.n <= 1) {
     LaunchTimer lt(st, name);
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr};
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, nullptr};
     k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
   {
     LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P};
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P, nullptr};
     k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
   }
@@ -1283,19 +1384,20 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
   }
   {
     LaunchTimer lt(st, name);
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr};
+    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
     k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
   }
   return TOPS_OK;
 }
 
-// Forward: o, ht and (in `saved`) qhat, kdec, A, D, chunk-start states h.
-int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
-        void* o, float* ht, void* saved, cudaStream_t st) {
+// Forward of a fixed-length (or padded varlen, blk_off != null) problem: o, ht and (in
+// `saved`) qhat, kdec, A, D, chunk-start states h.
+static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const float* h0, void* o, float* ht, void* saved, cudaStream_t st, const int32_t* blk_off) {
   if (g == nullptr) return fail(TOPS_ERR_UNSUPPORTED, "tc fwd needs gates");
   Saved sv;
-  carve_saved(s, saved, &sv);
+  carve_saved(s, saved, &sv, blk_off == nullptr);
   const int NTb = (s.T + BT - 1) / BT;
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   PrepMaps pm;
@@ -1324,7 +1426,7 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
     TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   }
-  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, "tc_scan");
+  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, "tc_scan", blk_off);
   if (rc) return rc;
   if (o == nullptr) return TOPS_OK;  // final state only
   {
@@ -1341,33 +1443,35 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
 
 static size_t dqk_smem() { return 2 * (size_t)DQK_STG + 1024; }
 
-size_t bwd_workspace(const tops_gla_shape& s, bool have_saved) {
+// workspace of bwd_core: dh states, span scratch, and the saved block when it is recomputed
+static size_t bwd_core_workspace(const tops_gla_shape& s, bool have_saved, bool spans) {
   const int NTb = (s.T + BT - 1) / BT;
   size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);  // dh states
-  n = (carve_spans(s, spans_for(s, NTb), nullptr, n, nullptr) + 1023) & ~size_t(1023);
-  if (!have_saved) n += saved_bytes(s);
+  if (spans) n = (carve_spans(s, spans_for(s, NTb), nullptr, n, nullptr) + 1023) & ~size_t(1023);
+  if (!have_saved) n += carve_saved(s, nullptr, nullptr, spans);
   return n;
 }
 
-// Backward: dq, dk, dv (bf16), dg (fp32), dh0 (fp32, optional) from the forward's saved block.
-int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
-        const void* dO, const float* dht, const void* saved_in, void* dq, void* dk, void* dv, float* dg, float* dh0,
-        void* workspace, cudaStream_t st) {
+// Backward of a fixed-length (or padded varlen, blk_off != null) problem: dq, dk, dv (bf16),
+// dg (fp32), dh0 (fp32, optional) from the forward's saved block.
+static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const float* h0, const void* dO, const float* dht, const void* saved_in, void* dq, void* dk,
+                    void* dv, float* dg, float* dh0, void* workspace, cudaStream_t st, const int32_t* blk_off) {
   const int NTb = (s.T + BT - 1) / BT;
   char* ws = static_cast<char*>(workspace);
   bf16* dhs = reinterpret_cast<bf16*>(ws);
   const size_t dh_bytes = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
-  const Spans spn = spans_for(s, NTb);
+  const Spans spn = blk_off ? Spans{1, NTb} : spans_for(s, NTb);
   SpanBufs sb;
   const size_t span_end = (carve_spans(s, spn, ws, dh_bytes, &sb) + 1023) & ~size_t(1023);
   void* saved = const_cast<void*>(saved_in);
   int rc;
   if (saved == nullptr) {  // recompute the forward intermediates (o is discarded into dv's buffer)
     saved = ws + span_end;
-    if ((rc = fwd(s, q, k, v, g, h0, dv, nullptr, saved, st))) return rc;
+    if ((rc = fwd_core(s, q, k, v, g, h0, dv, nullptr, saved, st, blk_off))) return rc;
   }
   Saved sv;
-  carve_saved(s, saved, &sv);
+  carve_saved(s, saved, &sv, blk_off == nullptr);
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   ScanMaps sm;
   bool okm = map_tok(&sm.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
@@ -1376,7 +1480,7 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
   const bool dh0_only = dq == nullptr;  // dq, dk, dv, dg all NULL: the reverse scan alone
   if (dh0_only) {
     if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
-    return run_scan(s, sm, 1, sv.D, dht, dh0, nullptr, sb, spn, st, "tc_scan_bwd");
+    return run_scan(s, sm, 1, sv.D, dht, dh0, nullptr, sb, spn, st, "tc_scan_bwd", blk_off);
   }
   OutMaps om;
   okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
@@ -1392,7 +1496,7 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
         map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
-  if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, "tc_scan_bwd"))) return rc;
+  if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, "tc_scan_bwd", blk_off))) return rc;
   {
     LaunchTimer lt(st, "tc_out_dv");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 1, static_cast<bf16*>(dv)};
@@ -1413,6 +1517,112 @@ int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
     TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
   }
   return TOPS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// public entry points: fixed-length problems run directly; packed varlen problems
+// (cu_seqlens, B == 1) are padded per segment to multiples of BT, run, and unpadded.
+// ---------------------------------------------------------------------------
+struct VarlenBufs {
+  char* q = nullptr;
+  char* k = nullptr;
+  char* v = nullptr;
+  char* g = nullptr;
+  char* x = nullptr;  // o (forward) or do (backward)
+  char* dq = nullptr;
+  char* dk = nullptr;
+  char* dv = nullptr;
+  char* dg = nullptr;
+  int32_t* blk = nullptr;
+};
+
+// padded copies of the token tensors (+ backward outputs) and the block offsets
+static size_t carve_varlen(const tops_gla_shape& s, bool bwd, char* base, VarlenBufs* vb) {
+  const size_t rows = (size_t)varlen_rows(s), H = (size_t)s.H;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    off = (off + 1023) & ~size_t(1023);
+    char* p = base ? base + off : nullptr;
+    off += bytes;
+    return p;
+  };
+  VarlenBufs b;
+  b.q = take(rows * H * s.K * 2);
+  b.k = take(rows * H * s.K * 2);
+  b.v = take(rows * H * s.V * 2);
+  b.g = take(rows * H * s.K * 4);
+  b.x = take(rows * H * s.V * 2);
+  if (bwd) {
+    b.dq = take(rows * H * s.K * 2);
+    b.dk = take(rows * H * s.K * 2);
+    b.dv = take(rows * H * s.V * 2);
+    b.dg = take(rows * H * s.K * 4);
+  }
+  b.blk = reinterpret_cast<int32_t*>(take(((size_t)s.N + 1) * 4));
+  if (vb) *vb = b;
+  return (off + 1023) & ~size_t(1023);
+}
+
+size_t fwd_workspace(const tops_gla_shape& s, bool own_saved) {
+  if (s.cu_seqlens == nullptr) return own_saved ? 0 : saved_bytes(s);
+  return carve_varlen(s, false, nullptr, nullptr) + (own_saved ? 0 : saved_bytes(s));
+}
+
+int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        void* o, float* ht, void* saved, void* workspace, cudaStream_t st) {
+  if (s.cu_seqlens == nullptr) return fwd_core(s, q, k, v, g, h0, o, ht, saved ? saved : workspace, st, nullptr);
+  if (g == nullptr) return fail(TOPS_ERR_UNSUPPORTED, "tc fwd needs gates");
+  char* ws = static_cast<char*>(workspace);
+  VarlenBufs vb;
+  const size_t used = carve_varlen(s, false, ws, &vb);
+  void* block = saved ? saved : ws + used;
+  const tops_gla_shape ps = padded_shape(s);
+  k_blk_off<<<1, 32, 0, st>>>(s.cu_seqlens, s.N, vb.blk);
+  TOPS_CUDA_LAUNCH_CHECK("tc varlen blocks");
+  const size_t H = (size_t)s.H;
+  int rc;
+  if ((rc = pad_rows(q, vb.q, H * s.K * 2, ps.T, s, vb.blk, 1, st)) || (rc = pad_rows(k, vb.k, H * s.K * 2, ps.T, s, vb.blk, 1, st)) ||
+      (rc = pad_rows(v, vb.v, H * s.V * 2, ps.T, s, vb.blk, 1, st)) || (rc = pad_rows(g, vb.g, H * s.K * 4, ps.T, s, vb.blk, 1, st)))
+    return rc;
+  if ((rc = fwd_core(ps, vb.q, vb.k, vb.v, reinterpret_cast<const float*>(vb.g), h0, o ? vb.x : nullptr, ht, block, st,
+                     vb.blk)))
+    return rc;
+  if (o) return pad_rows(vb.x, o, H * s.V * 2, s.T, s, vb.blk, 0, st);
+  return TOPS_OK;
+}
+
+size_t bwd_workspace(const tops_gla_shape& s, bool have_saved) {
+  if (s.cu_seqlens == nullptr) return bwd_core_workspace(s, have_saved, true);
+  return carve_varlen(s, true, nullptr, nullptr) + bwd_core_workspace(padded_shape(s), have_saved, false);
+}
+
+int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
+        const void* dO, const float* dht, const void* saved, void* dq, void* dk, void* dv, float* dg, float* dh0,
+        void* workspace, cudaStream_t st) {
+  if (s.cu_seqlens == nullptr)
+    return bwd_core(s, q, k, v, g, h0, dO, dht, saved, dq, dk, dv, dg, dh0, workspace, st, nullptr);
+  char* ws = static_cast<char*>(workspace);
+  VarlenBufs vb;
+  const size_t used = carve_varlen(s, true, ws, &vb);
+  const tops_gla_shape ps = padded_shape(s);
+  k_blk_off<<<1, 32, 0, st>>>(s.cu_seqlens, s.N, vb.blk);
+  TOPS_CUDA_LAUNCH_CHECK("tc varlen blocks");
+  const size_t H = (size_t)s.H;
+  int rc;
+  if ((rc = pad_rows(q, vb.q, H * s.K * 2, ps.T, s, vb.blk, 1, st)) || (rc = pad_rows(k, vb.k, H * s.K * 2, ps.T, s, vb.blk, 1, st)) ||
+      (rc = pad_rows(v, vb.v, H * s.V * 2, ps.T, s, vb.blk, 1, st)) || (rc = pad_rows(g, vb.g, H * s.K * 4, ps.T, s, vb.blk, 1, st)) ||
+      (rc = pad_rows(dO, vb.x, H * s.V * 2, ps.T, s, vb.blk, 1, st)))
+    return rc;
+  const bool grads = dq != nullptr;
+  if ((rc = bwd_core(ps, vb.q, vb.k, vb.v, reinterpret_cast<const float*>(vb.g), h0, vb.x, dht, saved,
+                     grads ? vb.dq : nullptr, grads ? vb.dk : nullptr, grads ? vb.dv : nullptr,
+                     grads ? reinterpret_cast<float*>(vb.dg) : nullptr, dh0, ws + used, st, vb.blk)))
+    return rc;
+  if (!grads) return TOPS_OK;
+  if ((rc = pad_rows(vb.dq, dq, H * s.K * 2, s.T, s, vb.blk, 0, st)) || (rc = pad_rows(vb.dk, dk, H * s.K * 2, s.T, s, vb.blk, 0, st)) ||
+      (rc = pad_rows(vb.dv, dv, H * s.V * 2, s.T, s, vb.blk, 0, st)))
+    return rc;
+  return pad_rows(vb.dg, dg, H * s.K * 4, s.T, s, vb.blk, 0, st);
 }
 
 }  // namespace tc

@@ -510,3 +510,39 @@ def test_pinned_host_fwd_bwd_matches_device_calls(gla):
     for nm, a, b in zip(("dq", "dk", "dv", "dg"), got, want[:4]):
         assert not a.is_cuda and a.is_pinned()
         assert_rel_l2(nm, a.float(), b.float().cpu(), 1e-3)
+
+
+@pytest.mark.parametrize("cu,H,K,V", [([0, 300, 301, 777, 1000], 2, 128, 256), ([0, 640, 1280], 1, 256, 128)],
+                         ids=["4seg", "2seg-aligned"])
+def test_tc_varlen_fwd_bwd_vs_oracle(gla, cu, H, K, V):
+    """Packed varlen (cu_seqlens) on the tensor-core path: segments padded to 128-row blocks
+    on the device, the state scans follow the segment boundaries; fwd + bwd vs the oracle."""
+    from tops import _C
+    from tops.ops.gla import _core
+    rng = np.random.default_rng(len(cu) * 7 + K)
+    T = cu[-1]
+    N = len(cu) - 1
+    q, k = (GC.bf16_round(rng.standard_normal((1, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((1, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((1, T, H, K))) / 16).astype(np.float32)
+    do = GC.bf16_round(rng.standard_normal((1, T, H, V), dtype=np.float32))
+    h0 = rng.standard_normal((N, H, K, V), dtype=np.float32)
+    dht = rng.standard_normal((N, H, K, V), dtype=np.float32)
+    bf = torch.bfloat16
+    cut = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    qt, kt, vt = (dev(x, bf).requires_grad_() for x in (q, k, v))
+    gt = dev(g).requires_grad_()
+    h0t = dev(h0).requires_grad_()
+    p = _core.make_plan(qt, V, 64, cut, K ** -0.5)
+    assert _core.saved_size(p, gt) > 0, "case should take the tensor-core path"
+    o, ht = gla.chunk_gla(qt, kt, vt, gt, initial_state=h0t, output_final_state=True, cu_seqlens=cut, chunk_size=64)
+    o_r, ht_r = O.chunk_gla(q, k, v, g, initial_state=h0, output_final_state=True, cu_seqlens=cu, chunk_size=64)
+    assert_rel_l2("o", o, o_r, BF16_L2)
+    assert_rel_l2("ht", ht, ht_r, BF16_L2)
+    ((o.float() * dev(do)).sum() + (ht * dev(dht)).sum()).backward()
+    dq_r, dk_r, dv_r, dg_r, dh0_r = O.chunk_gla_bwd(q, k, v, g, None, K ** -0.5, h0, None, None, do, dht, cu, 64)
+    for nm, got, want in (("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r), ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r),
+                          ("dh0", h0t.grad, dh0_r)):
+        assert_rel_l2(nm, got, want, BF16_L2)
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
