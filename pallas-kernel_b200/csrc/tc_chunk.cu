@@ -378,6 +378,7 @@ __device__ __forceinline__ uint32_t sw64(uint32_t row, uint32_t byte_in_row) {
   return row * 64u + ((((byte_in_row >> 4) ^ ((row >> 1) & 3u)) << 4) | (byte_in_row & 15u));
 }
 
+template <bool SEG>  // SEG: padded varlen problem, chunk ranges from p.blk_off
 __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMaps maps, ScanParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -389,7 +390,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   __shared__ uint32_t tmem_base;
 
   const int vt = blockIdx.x, h = blockIdx.y;
-  const bool seg = p.blk_off != nullptr;
+  constexpr bool seg = SEG;
   // b: batch index of the chunk data; sq: index of this CTA's initial / final state
   const int b = seg ? 0 : blockIdx.z / p.nspan, sp_ = seg ? 0 : blockIdx.z % p.nspan;
   const int sq = seg ? (int)blockIdx.z : b;
@@ -422,8 +423,8 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   constexpr uint32_t IDESC = ptx::idesc_bf16(128, 128, true, true);
 
   auto chunk_of = [&](int i) {
-    if (seg) return p.reverse ? i0 + n_it - 1 - i : i0 + i;
-    return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i;
+    if constexpr (SEG) return p.reverse ? i0 + n_it - 1 - i : i0 + i;
+    else return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i;
   };
   auto issue = [&](int i) {
     const int c = chunk_of(i);
@@ -434,7 +435,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     ptx::tma_load_4d(buf + (nkb + 1) * TILE_BYTES, &maps.y, v0 + 64, h, c * BT, b, &bar_full[i & 1]);
   };
   if (tid == 0) {
-    if (n_it > 0) issue(0);
+    if (!SEG || n_it > 0) issue(0);  // a varlen segment may be empty
     if (n_it > 1) issue(1);
   }
   // initial state -> TMEM buffer 0
@@ -532,7 +533,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     }
     // a failed wait in thread 0 leaves bar_mma pending: the next wait times out for everyone
   }
-  if (ok && n_it > 0) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
+  if (ok && (!SEG || n_it > 0)) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
   ptx::tc_fence_after();
   if (ok && active && p.span_decay && vt == 0)
     p.span_decay[((size_t)(sp_ * p.B + b) * p.H + h) * p.K + krow] = dprod;
@@ -1355,25 +1356,26 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
                     const int* blk_off = nullptr) {
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
-  if ((e = set_smem(k_scan, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
   if (blk_off != nullptr) {  // padded varlen problem: one CTA column per segment
+    if ((e = set_smem(k_scan<true>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, blk_off};
-    k_scan<<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
+    k_scan<true><<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
   if (spn.n <= 1) {
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, nullptr};
-    k_scan<<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+    k_scan<false><<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
   {
     LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P, nullptr};
-    k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
   }
   {
@@ -1385,7 +1387,7 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
   {
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
-    k_scan<<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
   }
   return TOPS_OK;
