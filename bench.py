@@ -554,36 +554,37 @@ def model_bench(args, world, rank, local, dev):
 
 
 def e2e_bench(args, world, dev, q, k, v, g, do, plan):
-    """Public API with HOST buffers: ``tops.ops.gla.chunk_gla_fwd_bwd_pinned`` copies q, k, v,
-    g, do in from pinned memory and dq, dk, dv, dg back out every step, one sequence slice
-    at a time on three streams (copy-in, compute, copy-out overlap)."""
+    """Public API with HOST buffers: ``tops.ops.gla.PinnedGLAPipeline`` copies q, k, v, g, do
+    in from pinned memory and dq, dk, dv, dg back out every step, one sequence slice at a
+    time on three streams (copy-in, compute, copy-out overlap, also across steps); the
+    timed region ends when the last step's gradients are in host memory."""
     import torch
 
-    from tops.ops.gla import chunk_gla_fwd_bwd_pinned
+    from tops.ops.gla import PinnedGLAPipeline
     hq, hk, hv, hg, hdo = (x.cpu().pin_memory() for x in (q, k, v, g, do))
     outs = tuple(torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (q, k, v, g))
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hg, hdo))
     d2h = sum(x.numel() * x.element_size() for x in outs)
-
-    def step():
-        chunk_gla_fwd_bwd_pinned(hq, hk, hv, hg, hdo, scale=plan.scale, chunk_size=plan.C, out=outs, device=dev)
+    pipe = PinnedGLAPipeline(plan.B, plan.T, plan.H, plan.K, plan.V, q.dtype, plan.scale, plan.C, device=dev)
 
     for _ in range(2):
-        step()
+        pipe.submit(hq, hk, hv, hg, hdo, outs)
+    pipe.synchronize()
     steps = max(3, min(args.steps, 10))
     barrier(world)
     s = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
     for _ in range(steps):
-        step()
+        pipe.submit(hq, hk, hv, hg, hdo, outs)
+    pipe.synchronize()  # the current stream now waits for the last copy-out
     e1.record(s)
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     tokens = plan.B * plan.T * world
     return {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": ms, "path": "tops.ops.gla.chunk_gla_fwd_bwd_pinned (C ABI chunk fwd+bwd per sequence "
-            "slice; pinned host inputs/outputs; copy-in / compute / copy-out on three streams)"}
+            "ms_per_step": ms, "path": "tops.ops.gla.PinnedGLAPipeline (C ABI chunk fwd+bwd per sequence slice; "
+            "pinned host inputs/outputs; copy-in / compute / copy-out on three streams, overlapped across steps)"}
 
 
 def main():

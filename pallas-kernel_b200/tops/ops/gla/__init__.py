@@ -16,10 +16,11 @@ from .chunk import (
 )
 from .fused_chunk import fused_chunk_gla
 from .fused_recurrent import fused_recurrent_gla, fused_recurrent_gla_bwd
-from .host import chunk_gla_fwd_bwd_pinned
+from .host import PinnedGLAPipeline, chunk_gla_fwd_bwd_pinned
 
 __all__ = [
     "chunk_gla_fwd_bwd_pinned",
+    "PinnedGLAPipeline",
     "naive_recurrent_gla",
     "chunk_gla",
     "chunk_local_cumsum",

@@ -5,8 +5,10 @@ entry point for callers that keep activations in host memory (offloaded training
 a host-side framework).  The batch is cut into slices of whole sequences; three CUDA
 streams overlap the host->device copy of slice i+1, the fused forward + backward of
 slice i on this library's kernels, and the device->host copy of slice i-1's gradients,
-so the step costs about the slower PCIe direction instead of the sum of both
-directions plus the compute.  Sequences are independent, so slicing is exact.
+so a step costs about the slower PCIe direction instead of the sum of both directions
+plus the compute.  ``PinnedGLAPipeline`` keeps its device ring and streams between
+calls, so consecutive steps overlap too (step n+1's inputs go in while step n's
+gradients come out).  Sequences are independent, so slicing is exact.
 """
 from __future__ import annotations
 
@@ -14,17 +16,88 @@ import torch
 
 from . import _core
 
-__all__ = ["chunk_gla_fwd_bwd_pinned"]
+__all__ = ["chunk_gla_fwd_bwd_pinned", "PinnedGLAPipeline"]
 
 
-class _Ring:
-    """`depth` device copies of a set of per-slice buffers."""
+class PinnedGLAPipeline:
+    """Reusable copy-in / compute / copy-out pipeline for one problem shape.
 
-    def __init__(self, shapes_dtypes, depth, dev):
-        self.bufs = [[torch.empty(s, dtype=d, device=dev) for s, d in shapes_dtypes] for _ in range(depth)]
+    ``submit(q, k, v, g, do, out)`` enqueues one step (host tensors, pinned) and returns
+    at once; ``synchronize()`` waits until every submitted step's gradients are in
+    ``out``.  Slices of ``slice_batch`` sequences rotate through ``depth`` device slots.
+    """
 
-    def __getitem__(self, i):
-        return self.bufs[i % len(self.bufs)]
+    def __init__(self, B, T, H, K, V, dtype=torch.bfloat16, scale=None, chunk_size: int = 64,
+                 slice_batch: int = 1, depth: int = 3, device=None):
+        self.dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.B, self.T, self.H, self.K, self.V = B, T, H, K, V
+        self.dtype = dtype
+        self.scale = K ** -0.5 if scale is None else scale
+        self.C = chunk_size
+        self.sb = max(1, min(slice_batch, B))
+        self.depth = max(1, depth)
+        sb, dev = self.sb, self.dev
+        mk = lambda d, dt: torch.empty(sb, T, H, d, dtype=dt, device=dev)
+        self.ins = [[mk(K, dtype), mk(K, dtype), mk(V, dtype), mk(K, torch.float32), mk(V, dtype)]
+                    for _ in range(self.depth)]
+        self.outs = [[mk(K, dtype), mk(K, dtype), mk(V, dtype), mk(K, torch.float32)] for _ in range(self.depth)]
+        self.s_in, self.s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        self.s_comp = torch.cuda.Stream(dev)
+        self.ev_in = [torch.cuda.Event() for _ in range(self.depth)]
+        self.ev_comp = [torch.cuda.Event() for _ in range(self.depth)]
+        self.ev_out = [torch.cuda.Event() for _ in range(self.depth)]
+        self.used = [False] * self.depth
+        self.count = 0  # slices submitted so far
+        self.plans = {}
+
+    def _plan(self, qd, n):
+        p = self.plans.get(n)
+        if p is None:
+            p = self.plans[n] = _core.make_plan(qd, self.V, self.C, None, self.scale)
+        return p
+
+    def submit(self, q, k, v, g, do, out):
+        B = q.shape[0]
+        if tuple(q.shape) != (self.B, self.T, self.H, self.K):
+            raise ValueError(f"pipeline built for {(self.B, self.T, self.H, self.K)}, got {tuple(q.shape)}")
+        dq_h, dk_h, dv_h, dg_h = out
+        for b0 in range(0, B, self.sb):
+            b1 = min(B, b0 + self.sb)
+            n = b1 - b0
+            slot = self.count % self.depth
+            # host -> device (the slot is free once the compute that last read it is done)
+            with torch.cuda.stream(self.s_in):
+                if self.used[slot]:
+                    self.s_in.wait_event(self.ev_comp[slot])
+                dst = [t[:n] for t in self.ins[slot]]
+                for d, src in zip(dst, (q, k, v, g, do)):
+                    d.copy_(src[b0:b1], non_blocking=True)
+                self.ev_in[slot].record(self.s_in)
+            with torch.cuda.stream(self.s_comp):
+                self.s_comp.wait_event(self.ev_in[slot])
+                if self.used[slot]:
+                    self.s_comp.wait_event(self.ev_out[slot])  # its last gradients have left the slot
+                qd, kd, vd, gd, dod = dst
+                p = self._plan(qd, n)
+                o, _, sv = _core.chunk_fwd(p, qd, kd, vd, gd, None, False, save=True)
+                ob = [t[:n] for t in self.outs[slot]]
+                _core.chunk_bwd(p, qd, kd, vd, gd, None, dod, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
+                                False, block=sv.get("block"), out=ob)
+                self.ev_comp[slot].record(self.s_comp)
+            # device -> host
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(self.ev_comp[slot])
+                for d, src in zip((dq_h, dk_h, dv_h, dg_h), ob):
+                    d[b0:b1].copy_(src, non_blocking=True)
+                self.ev_out[slot].record(self.s_out)
+            self.used[slot] = True
+            self.count += 1
+        return out
+
+    def synchronize(self):
+        self.s_out.synchronize()
+        cur = torch.cuda.current_stream(self.dev)
+        cur.wait_stream(self.s_out)
 
 
 def chunk_gla_fwd_bwd_pinned(q, k, v, g, do, scale=None, chunk_size: int = 64, slice_batch: int = 1,
@@ -41,58 +114,13 @@ def chunk_gla_fwd_bwd_pinned(q, k, v, g, do, scale=None, chunk_size: int = 64, s
     for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("do", do)):
         if not t.is_pinned():
             raise ValueError(f"{name} must be in pinned host memory")
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     B, T, H, K = q.shape
     V = v.shape[-1]
-    if scale is None:
-        scale = K ** -0.5
     if out is None:
         out = (torch.empty_like(q).pin_memory(), torch.empty_like(k).pin_memory(), torch.empty_like(v).pin_memory(),
                torch.empty(B, T, H, K, dtype=torch.float32).pin_memory())
-    dq_h, dk_h, dv_h, dg_h = out
-    sb = max(1, min(slice_batch, B))
-    nsl = (B + sb - 1) // sb
-    depth = max(1, min(depth, nsl))
-    ins = _Ring([((sb, T, H, K), q.dtype), ((sb, T, H, K), k.dtype), ((sb, T, H, V), v.dtype),
-                 ((sb, T, H, K), torch.float32), ((sb, T, H, V), do.dtype)], depth, dev)
-    outs = _Ring([((sb, T, H, K), q.dtype), ((sb, T, H, K), k.dtype), ((sb, T, H, V), v.dtype),
-                  ((sb, T, H, K), torch.float32)], depth, dev)
-    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    s_comp = torch.cuda.current_stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(nsl)]
-    ev_comp = [torch.cuda.Event() for _ in range(nsl)]
-    ev_out = [torch.cuda.Event() for _ in range(nsl)]
-    plans = {}
-    for i in range(nsl):
-        b0, b1 = i * sb, min(B, (i + 1) * sb)
-        n = b1 - b0
-        # host -> device (slot i % depth is free once slice i - depth's compute has read it)
-        with torch.cuda.stream(s_in):
-            if i >= depth:
-                s_in.wait_event(ev_comp[i - depth])
-            dst = [t[:n] for t in ins[i]]
-            for d, src in zip(dst, (q, k, v, g, do)):
-                d.copy_(src[b0:b1], non_blocking=True)
-            ev_in[i].record(s_in)
-        # compute on the current stream
-        s_comp.wait_event(ev_in[i])
-        if i >= depth:
-            s_comp.wait_event(ev_out[i - depth])  # slice i - depth's gradients have left the ring slot
-        qd, kd, vd, gd, dod = dst
-        p = plans.get(n)
-        if p is None:
-            p = plans[n] = _core.make_plan(qd, V, chunk_size, None, scale)
-        o, _, sv = _core.chunk_fwd(p, qd, kd, vd, gd, None, False, save=True)
-        ob = [t[:n] for t in outs[i]]
-        _core.chunk_bwd(p, qd, kd, vd, gd, None, dod, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"), False,
-                        block=sv.get("block"), out=ob)
-        ev_comp[i].record(s_comp)
-        # device -> host
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_comp[i])
-            for d, src in zip((dq_h, dk_h, dv_h, dg_h), ob):
-                d[b0:b1].copy_(src, non_blocking=True)
-            ev_out[i].record(s_out)
-    s_comp.wait_stream(s_out)
-    s_out.synchronize()
-    return dq_h, dk_h, dv_h, dg_h
+    pipe = PinnedGLAPipeline(B, T, H, K, V, q.dtype, scale, chunk_size, slice_batch,
+                             min(depth, (B + slice_batch - 1) // max(1, slice_batch)), device)
+    pipe.submit(q, k, v, g, do, out)
+    pipe.synchronize()
+    return out

@@ -546,3 +546,38 @@ def test_tc_varlen_fwd_bwd_vs_oracle(gla, cu, H, K, V):
         assert_rel_l2(nm, got, want, BF16_L2)
     torch.cuda.synchronize()
     assert _C.lib().tops_gla_device_error() == 0
+
+
+def test_pinned_pipeline_back_to_back_steps(gla):
+    """Two steps submitted back to back through one PinnedGLAPipeline (ring slots reused
+    across the steps) give each step's own gradients."""
+    from tops.ops.gla import _core
+    torch.manual_seed(10)
+    B, T, H, K, V = 3, 300, 1, 128, 128
+    bf = torch.bfloat16
+
+    def inputs():
+        q, k = (torch.randn(B, T, H, K).to(bf).pin_memory() for _ in range(2))
+        v = torch.randn(B, T, H, V).to(bf).pin_memory()
+        g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K)) / 16).pin_memory()
+        do = torch.randn(B, T, H, V).to(bf).pin_memory()
+        return q, k, v, g, do
+
+    def out_buffers():
+        return (torch.empty(B, T, H, K, dtype=bf).pin_memory(), torch.empty(B, T, H, K, dtype=bf).pin_memory(),
+                torch.empty(B, T, H, V, dtype=bf).pin_memory(), torch.empty(B, T, H, K).pin_memory())
+
+    steps = [inputs(), inputs()]
+    outs = [out_buffers(), out_buffers()]
+    pipe = gla.PinnedGLAPipeline(B, T, H, K, V, bf, depth=2)
+    for x, o in zip(steps, outs):
+        pipe.submit(*x, o)
+    pipe.synchronize()
+    for x, o in zip(steps, outs):
+        qd, kd, vd, gd, dod = (t.cuda() for t in x)
+        p = _core.make_plan(qd, V, 64, None, K ** -0.5)
+        _, _, sv = _core.chunk_fwd(p, qd, kd, vd, gd, None, False, save=True)
+        want = _core.chunk_bwd(p, qd, kd, vd, gd, None, dod, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
+                               False, block=sv.get("block"))
+        for nm, a, b in zip(("dq", "dk", "dv", "dg"), o, want[:4]):
+            assert_rel_l2(nm, a.float(), b.float().cpu(), 1e-3)
