@@ -56,7 +56,8 @@ enum tops_status {
   TOPS_ERR_UNSUPPORTED = -2,  /* valid request this build cannot serve (e.g. no sm_100 device) */
   TOPS_ERR_CUDA = -3,         /* a CUDA runtime call failed */
   TOPS_ERR_WORKSPACE = -4,    /* workspace missing or smaller than *_workspace_size() */
-  TOPS_ERR_TIMEOUT = -5       /* a bounded device-side wait gave up */
+  TOPS_ERR_TIMEOUT = -5,      /* a bounded device-side wait gave up */
+  TOPS_ERR_NCCL = -6          /* an NCCL call failed */
 };
 
 /* Problem description shared by every chunked entry point. */
@@ -259,6 +260,39 @@ TOPS_API int tops_gla_span_decay(const tops_gla_shape* s, const float* g, float*
  * out may alias s_local. */
 TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, const float* decay, const float* h_in,
                            const float* s_local, float* out, void* stream);
+
+/* ---- sequence-parallel state exchange over NCCL ---------
+ * Every rank holds one contiguous span of a long sequence.  Forward (backward = 0):
+ * local_state = the span's final state from a zero state S [N,H,K,V] (tops_gla_chunk_fwd
+ * with o == NULL), decay = exp(sum of the span's gates) D [N,H,K] (tops_gla_span_decay),
+ * boundary = the sequence's initial state h0 or NULL; out = this rank's incoming state
+ * (prefix H_0 = h0, H_{r+1} = D_r H_r + S_r), total = the whole sequence's final state
+ * (optional).  Backward (backward = 1): local_state = the gradient w.r.t. this span's
+ * incoming state from its own loss (tops_gla_chunk_bwd with NULL gradients and dht = NULL),
+ * boundary = dht or NULL; out = the final-state gradient this rank's backward must use
+ * (suffix G_{R-1} = dht, G_{r-1} = D_r G_r + L_r).  One ncclAllGather on `stream`, then one
+ * kernel; all fp32.  The reference has no multi-device code (its scan is
+ * tops/ops/common/chunk_h.py:372-386; this is its exact linear decomposition).  `comm` is an
+ * ncclComm_t; NCCL is loaded at run time (libnccl.so.2), TOPS_ERR_UNSUPPORTED without it. */
+typedef struct tops_gla_exchange_args {
+  void* comm;
+  int32_t rank, world;
+  int32_t N, H, K, V;
+  int32_t backward;
+  const float* local_state;
+  const float* decay;
+  const float* boundary;
+  float* out;
+  float* total;
+  void* workspace; size_t workspace_bytes;
+} tops_gla_exchange_args;
+TOPS_API size_t tops_gla_state_exchange_workspace_size(const tops_gla_exchange_args* a);
+TOPS_API int tops_gla_state_exchange(const tops_gla_exchange_args* a, void* stream);
+/* Communicator helpers for hosts without their own: id is NCCL's 128-byte unique id
+ * (created on one rank, broadcast by the host, passed to every rank). */
+TOPS_API int tops_gla_nccl_get_unique_id(void* id);
+TOPS_API int tops_gla_nccl_comm_init(void** comm, int32_t world, const void* id, int32_t rank);
+TOPS_API int tops_gla_nccl_comm_destroy(void* comm);
 
 /* ---- GLA layer pieces around the chunked op ------------ */
 

@@ -32,9 +32,28 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+def nccl_include() -> str | None:
+    """Directory of nccl.h (the nvidia-nccl wheel torch ships with, or the system's)."""
+    try:
+        import nvidia.nccl as n  # type: ignore
+        for p in n.__path__:
+            if (Path(p) / "include" / "nccl.h").exists():
+                return str(Path(p) / "include")
+    except ImportError:
+        pass
+    for p in ("/usr/include", "/usr/local/cuda/include"):
+        if (Path(p) / "nccl.h").exists():
+            return p
+    return None
+
+
 def _flags(debug: bool) -> list[str]:
     f = ARCH + ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
                 "--expt-relaxed-constexpr", "-I", str(INC), "-I", str(CSRC)]
+    inc = nccl_include()
+    if inc is None:
+        raise RuntimeError("nccl.h not found (needed for the state-exchange entry points)")
+    f += ["-I", inc]
     if debug:
         f += ["-DTOPS_DEBUG=1"]
     return f

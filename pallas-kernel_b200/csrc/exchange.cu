@@ -1,0 +1,158 @@
+// Sequence-parallel state exchange over NCCL.  Each rank holds one
+// contiguous span of a long sequence.  The chunked scan is linear in its initial state
+// (tops/ops/common/chunk_h.py:372-386): a span's final state is D * H_in + S, with S its
+// final state from a zero state and D = exp(sum of its gates) (diagonal in K).
+//  * forward: all ranks all-gather (S_r, D_r); rank r's incoming state is the prefix
+//    H_0 = h0 (or 0), H_{r+1} = D_r H_r + S_r, and the whole sequence's final state is H_R;
+//  * backward: all ranks all-gather (L_r, D_r), L_r = the gradient w.r.t. rank r's incoming
+//    state from its own loss; rank r's final-state gradient is the suffix
+//    G_{R-1} = dht (or 0), G_{r-1} = D_r G_r + L_r.
+// One ncclAllGather of a packed (state | decay) buffer, then one elementwise kernel.  NCCL is
+// loaded at run time (dlopen of libnccl.so.2; the torch process has it loaded already) so
+// the library has no link-time NCCL dependency and loads on hosts without it.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace tops {
+namespace exchange {
+
+struct Nccl {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static const Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+    if (!h) return;
+    n.get_unique_id = reinterpret_cast<decltype(n.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    n.comm_init_rank = reinterpret_cast<decltype(n.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
+    n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
+    n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_gather && n.error_string;
+  });
+  return n;
+}
+
+static int nccl_status(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return TOPS_OK;
+  return fail(TOPS_ERR_NCCL, std::string(what) + ": " + nccl().error_string(r));
+}
+
+// packed per rank: [state N*H*K*V | decay N*H*K], fp32
+__global__ void k_pack(size_t ns, size_t nd, const float* __restrict__ s, const float* __restrict__ d,
+                       float* __restrict__ out) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns + nd; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = i < ns ? s[i] : d[i - ns];
+}
+
+// forward: out = H_rank, total = H_R; backward: out = G_rank (suffix), total unused
+__global__ void k_combine(int world, int rank, int backward, size_t ns, int V, const float* __restrict__ gathered,
+                          const float* __restrict__ boundary, float* __restrict__ out, float* __restrict__ total) {
+  const size_t per = ns + ns / V;  // floats per rank
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / V;  // (n*H + h)*K + k
+    float x = boundary ? boundary[i] : 0.f;
+    if (!backward) {
+      for (int r = 0; r < world; ++r) {
+        if (r == rank) out[i] = x;
+        const float* g = gathered + (size_t)r * per;
+        x = fmaf(g[ns + row], x, g[i]);
+      }
+      if (total) total[i] = x;
+    } else {
+      for (int r = world - 1; r > rank; --r) {
+        const float* g = gathered + (size_t)r * per;
+        x = fmaf(g[ns + row], x, g[i]);
+      }
+      out[i] = x;
+    }
+  }
+}
+
+}  // namespace exchange
+}  // namespace tops
+
+using namespace tops;
+using namespace tops::exchange;
+
+extern "C" {
+
+TOPS_API int tops_gla_nccl_get_unique_id(void* id) {
+  TOPS_CHECK_ARG(id, "nccl_get_unique_id: id buffer is required");
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  ncclUniqueId u;
+  int rc = nccl_status(nccl().get_unique_id(&u), "ncclGetUniqueId");
+  if (rc == TOPS_OK) std::memcpy(id, &u, sizeof(u));
+  return rc;
+}
+
+TOPS_API int tops_gla_nccl_comm_init(void** comm, int32_t world, const void* id, int32_t rank) {
+  TOPS_CHECK_ARG(comm && id && world > 0 && rank >= 0 && rank < world, "nccl_comm_init: bad arguments");
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclComm_t c = nullptr;
+  const int rc = nccl_status(nccl().comm_init_rank(&c, world, u, rank), "ncclCommInitRank");
+  *comm = c;
+  return rc;
+}
+
+TOPS_API int tops_gla_nccl_comm_destroy(void* comm) {
+  if (comm == nullptr) return TOPS_OK;
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  return nccl_status(nccl().comm_destroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy");
+}
+
+TOPS_API size_t tops_gla_state_exchange_workspace_size(const tops_gla_exchange_args* a) {
+  if (!a || a->world <= 0 || a->N <= 0 || a->H <= 0 || a->K <= 0 || a->V <= 0) return 0;
+  const size_t ns = (size_t)a->N * a->H * a->K * a->V, nd = (size_t)a->N * a->H * a->K;
+  return (size_t)(a->world + 1) * (ns + nd) * sizeof(float);
+}
+
+TOPS_API int tops_gla_state_exchange(const tops_gla_exchange_args* a, void* stream) {
+  TOPS_CHECK_ARG(a, "state_exchange: args are required");
+  TOPS_CHECK_ARG(a->comm && a->world > 0 && a->rank >= 0 && a->rank < a->world, "state_exchange: bad communicator");
+  TOPS_CHECK_ARG(a->N > 0 && a->H > 0 && a->K > 0 && a->V > 0, "state_exchange: bad shape");
+  TOPS_CHECK_ARG(a->local_state && a->decay && a->out, "state_exchange: local_state, decay and out are required");
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  const size_t need = tops_gla_state_exchange_workspace_size(a);
+  if (a->workspace == nullptr || a->workspace_bytes < need)
+    return fail(TOPS_ERR_WORKSPACE, "state_exchange: workspace smaller than tops_gla_state_exchange_workspace_size()");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t ns = (size_t)a->N * a->H * a->K * a->V, nd = (size_t)a->N * a->H * a->K;
+  float* send = static_cast<float*>(a->workspace);
+  float* gathered = send + ns + nd;
+  const int blocks = (int)((ns + nd + 255) / 256 < 4096 ? (ns + nd + 255) / 256 : 4096);
+  {
+    LaunchTimer lt(st, "exchange_pack");
+    k_pack<<<blocks, 256, 0, st>>>(ns, nd, a->local_state, a->decay, send);
+    TOPS_CUDA_LAUNCH_CHECK("state_exchange pack");
+  }
+  int rc = nccl_status(nccl().all_gather(send, gathered, ns + nd, ncclFloat32, static_cast<ncclComm_t>(a->comm), st),
+                       "ncclAllGather");
+  if (rc) return rc;
+  {
+    LaunchTimer lt(st, "exchange_combine");
+    const int cb = (int)((ns + 255) / 256 < 4096 ? (ns + 255) / 256 : 4096);
+    k_combine<<<cb, 256, 0, st>>>(a->world, a->rank, a->backward, ns, a->V, gathered, a->boundary, a->out,
+                                  a->backward ? nullptr : a->total);
+    TOPS_CUDA_LAUNCH_CHECK("state_exchange combine");
+  }
+  return TOPS_OK;
+}
+
+}  // extern "C"

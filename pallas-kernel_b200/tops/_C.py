@@ -68,6 +68,13 @@ class XlaDesc(C.Structure):
                 ("reverse", C.c_int32), ("saved_bytes", C.c_uint64), ("workspace_bytes", C.c_uint64)]
 
 
+class ExchangeArgs(C.Structure):
+    _fields_ = [("comm", C.c_void_p), ("rank", C.c_int32), ("world", C.c_int32), ("N", C.c_int32), ("H", C.c_int32),
+                ("K", C.c_int32), ("V", C.c_int32), ("backward", C.c_int32), ("local_state", C.c_void_p),
+                ("decay", C.c_void_p), ("boundary", C.c_void_p), ("out", C.c_void_p), ("total", C.c_void_p),
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
 VP, I32, F32C = C.c_void_p, C.c_int32, C.c_float
 SIGNATURES = {
     "tops_gla_last_error": (C.c_char_p, []),
@@ -106,6 +113,11 @@ SIGNATURES = {
                                          VP]),
     "tops_gla_gate_logsigmoid_fwd": (C.c_int, [C.c_int64, I32, F32C, F32C, I32, VP, VP, VP]),
     "tops_gla_gate_logsigmoid_bwd": (C.c_int, [C.c_int64, I32, F32C, F32C, I32, VP, VP, VP, VP]),
+    "tops_gla_state_exchange_workspace_size": (C.c_size_t, [C.POINTER(ExchangeArgs)]),
+    "tops_gla_state_exchange": (C.c_int, [C.POINTER(ExchangeArgs), VP]),
+    "tops_gla_nccl_get_unique_id": (C.c_int, [VP]),
+    "tops_gla_nccl_comm_init": (C.c_int, [C.POINTER(C.c_void_p), I32, VP, I32]),
+    "tops_gla_nccl_comm_destroy": (C.c_int, [VP]),
     "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),

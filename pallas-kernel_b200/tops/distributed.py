@@ -24,13 +24,63 @@ defaults use this library's kernels.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
 
 __all__ = ["shard", "prefix_states", "suffix_grads", "all_gather_stack", "seq_parallel_forward",
-           "seq_parallel_backward", "chunk_gla_seq_parallel"]
+           "seq_parallel_backward", "chunk_gla_seq_parallel", "NcclStateExchange"]
+
+
+class NcclStateExchange:
+    """The C ABI's state exchange (``tops_gla_state_exchange``: one ncclAllGather of the
+    packed (state, decay) pairs and one prefix / suffix kernel) on a communicator of this
+    library's own; ``group`` only broadcasts NCCL's unique id.  Every rank of the group must
+    construct it (communicator creation is collective)."""
+
+    def __init__(self, group=None):
+        from . import _C
+        self._C = _C
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        idbuf = (ctypes.c_char * 128)()
+        if self.rank == 0:
+            _C.call("tops_gla_nccl_get_unique_id", ctypes.addressof(idbuf))
+        obj = [bytes(idbuf)]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        ctypes.memmove(idbuf, obj[0], 128)
+        self.comm = ctypes.c_void_p()
+        _C.call("tops_gla_nccl_comm_init", ctypes.byref(self.comm), self.world, ctypes.addressof(idbuf), self.rank)
+
+    def _run(self, backward: bool, local: torch.Tensor, decay: torch.Tensor, boundary, want_total: bool):
+        C = self._C
+        local = local.float().contiguous()
+        decay = decay.float().contiguous()
+        boundary = None if boundary is None else boundary.float().contiguous()
+        N, H, K, V = local.shape
+        out = torch.empty_like(local)
+        total = torch.empty_like(local) if want_total else None
+        a = C.ExchangeArgs(self.comm, self.rank, self.world, N, H, K, V, int(backward), C.ptr(local), C.ptr(decay),
+                           C.ptr(boundary), C.ptr(out), C.ptr(total), None, 0)
+        n = int(C.lib().tops_gla_state_exchange_workspace_size(a))
+        ws = torch.empty(n, dtype=torch.uint8, device=local.device)
+        a.workspace, a.workspace_bytes = C.ptr(ws), n
+        C.call("tops_gla_state_exchange", a, C.stream_of(local))
+        return out, total
+
+    def forward(self, S, D, h0=None):
+        """-> (this rank's incoming state, the whole sequence's final state)."""
+        return self._run(False, S, D, h0, True)
+
+    def backward(self, L, D, dht=None):
+        """-> the final-state gradient this rank's backward must use."""
+        return self._run(True, L, D, dht, False)[0]
+
+    def close(self):
+        if self.comm:
+            self._C.call("tops_gla_nccl_comm_destroy", self.comm)
+            self.comm = ctypes.c_void_p()
 
 
 def shard(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
@@ -81,19 +131,24 @@ def suffix_grads(dh0_local: torch.Tensor, D: torch.Tensor, dht: torch.Tensor | N
 
 
 def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, h0=None, group=None,
-                         local_final: Callable | None = None):
+                         local_final: Callable | None = None, exchange: NcclStateExchange | None = None):
     """Forward of one rank's span.
 
     local_fwd(q, k, v, g, h0) -> (o, final_state) runs the chunked forward on this span;
     span_decay(g) -> D [N, H, K] is exp of the span's gate sums; local_final(q, k, v, g)
     -> the span's final state from a zero state (default: local_fwd's).  ``h0`` (rank 0's
-    initial state) is read on every rank (pass the same tensor or None).  Returns
-    (o, H_in, ht_global) where H_in is this rank's incoming state and ht_global the final
-    state of the whole sequence (identical on all ranks).
+    initial state) is read on every rank (pass the same tensor or None).  ``exchange``: use the
+    C ABI's NCCL exchange instead of torch all-gathers.  Returns (o, H_in, ht_global) where
+    H_in is this rank's incoming state and ht_global the final state of the whole sequence
+    (identical on all ranks).
     """
     rank = dist.get_rank(group)
     S = local_final(q, k, v, g) if local_final is not None else local_fwd(q, k, v, g, None)[1]
     D = span_decay(g)
+    if exchange is not None:
+        H_in, ht_global = exchange.forward(S, D, h0)
+        o, _ = local_fwd(q, k, v, g, H_in)
+        return o, H_in, ht_global
     S_all = all_gather_stack(S, group)
     D_all = all_gather_stack(D.to(S.dtype), group)
     H_all = prefix_states(S_all, D_all, h0)
@@ -104,7 +159,7 @@ def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, 
 
 
 def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=None, group=None,
-                          local_dh0: Callable | None = None):
+                          local_dh0: Callable | None = None, exchange: NcclStateExchange | None = None):
     """Backward of one rank's span.
 
     local_bwd(H_in, do, dht) -> (dq, dk, dv, dg, dh0) runs the chunked backward of this span
@@ -115,6 +170,8 @@ def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=No
     """
     rank = dist.get_rank(group)
     dh0_local = local_dh0(H_in, do) if local_dh0 is not None else local_bwd(H_in, do, None)[-1]
+    if exchange is not None:
+        return local_bwd(H_in, do, exchange.backward(dh0_local, D, dht))
     L_all = all_gather_stack(dh0_local, group)
     D_all = all_gather_stack(D.to(dh0_local.dtype), group)
     G_all = suffix_grads(L_all, D_all, dht)
@@ -123,7 +180,7 @@ def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=No
 
 class _SeqParallelChunkGLA(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, g, h0, scale, chunk_size, group):
+    def forward(ctx, q, k, v, g, h0, scale, chunk_size, group, exchange):
         from .ops.gla import _core
 
         p = _core.make_plan(q, v.shape[-1], chunk_size, None, scale)
@@ -138,10 +195,10 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
             return _core.final_state(p, q_, k_, v_, g_, None)
 
         o, H_in, ht = seq_parallel_forward(local_fwd, lambda g_: _core.span_decay(p, g_), q, k, v, g, h0, group,
-                                           local_final=local_final)
+                                           local_final=local_final, exchange=exchange)
         ctx.save_for_backward(q, k, v, g, H_in)
         ctx.fwd_saved = saved
-        ctx.plan, ctx.group, ctx.has_h0 = p, group, h0 is not None
+        ctx.plan, ctx.group, ctx.has_h0, ctx.exchange = p, group, h0 is not None, exchange
         return o, ht
 
     @staticmethod
@@ -161,21 +218,23 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
         D = _core.span_decay(p, g)
         dq, dk, dv, dg, dh0 = seq_parallel_backward(local_bwd, D, H_in, do.contiguous().to(q.dtype),
                                                     None if dht is None else dht.float(), ctx.group,
-                                                    local_dh0=local_dh0)
+                                                    local_dh0=local_dh0, exchange=ctx.exchange)
         rank = dist.get_rank(ctx.group)
         d_h0 = dh0 if (ctx.has_h0 and rank == 0) else None
-        return dq, dk, dv, dg, d_h0, None, None, None
+        return dq, dk, dv, dg, d_h0, None, None, None, None
 
 
-def chunk_gla_seq_parallel(q, k, v, g, scale=None, initial_state=None, chunk_size=64, group=None):
+def chunk_gla_seq_parallel(q, k, v, g, scale=None, initial_state=None, chunk_size=64, group=None, exchange=None):
     """chunk_gla over a sequence split into contiguous spans, one per rank (differentiable).
 
     q, k, g: this rank's span [B, T_r, H, K]; v: [B, T_r, H, V] (CUDA tensors, same T_r on
     every rank).  initial_state: [B, H, K, V] state before rank 0's span (or None).
     Returns (o of this span, final state of the whole sequence).  The only communication
-    is two all-gathers of [B, H, K, V] fp32 states (+ [B, H, K] decays) per direction.
+    is two all-gathers of [B, H, K, V] fp32 states (+ [B, H, K] decays) per direction
+    (torch.distributed, or the C ABI's NCCL exchange when ``exchange`` is an
+    ``NcclStateExchange``).
     """
     if scale is None:
         scale = q.shape[-1] ** -0.5
     return _SeqParallelChunkGLA.apply(q, k, v, g.float().contiguous(), initial_state, float(scale), int(chunk_size),
-                                      group)
+                                      group, exchange)

@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol(lib):
 def test_struct_layouts_match_ctypes(lib, tmp_path):
     """Compile a C probe against the header and compare sizeof/offsetof with ctypes."""
     structs = {"tops_gla_shape": lib.Shape, "tops_gla_chunk_fwd_args": lib.ChunkFwdArgs,
-               "tops_gla_xla_desc": lib.XlaDesc,
+               "tops_gla_xla_desc": lib.XlaDesc, "tops_gla_exchange_args": lib.ExchangeArgs,
                "tops_gla_chunk_bwd_args": lib.ChunkBwdArgs, "tops_gla_recurrent_args": lib.RecArgs,
                "tops_gla_recurrent_bwd_args": lib.RecBwdArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]

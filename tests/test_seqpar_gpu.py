@@ -44,7 +44,7 @@ def _inputs(dev):
     return q, k, v, g.contiguous(), h0, do, dht
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, use_exchange=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     sys.path[:0] = [str(ROOT), str(ROOT / "pallas-kernel_b200")]
     import datetime
@@ -59,7 +59,8 @@ def _worker(rank, world, port, out):
     sl = slice(rank * T // world, (rank + 1) * T // world)
     qs, ks, vs, gs = (x[:, sl].contiguous().requires_grad_() for x in (q, k, v, g))
     h0r = h0.clone().requires_grad_()
-    o, ht = TD.chunk_gla_seq_parallel(qs, ks, vs, gs, initial_state=h0r, chunk_size=64)
+    ex = TD.NcclStateExchange() if use_exchange else None
+    o, ht = TD.chunk_gla_seq_parallel(qs, ks, vs, gs, initial_state=h0r, chunk_size=64, exchange=ex)
     loss = (o.float() * do[:, sl].float()).sum() + (ht * dht).sum()  # ht and dht are replicated
     loss.backward()
     res = dict(o=o.detach().cpu(), ht=ht.detach().cpu(), dq=qs.grad.cpu(), dk=ks.grad.cpu(), dv=vs.grad.cpu(),
@@ -67,19 +68,23 @@ def _worker(rank, world, port, out):
     if rank == 0:
         res["dh0"] = h0r.grad.cpu()
     out[rank] = res
+    if ex is not None:
+        torch.cuda.synchronize()
+        ex.close()
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.timeout(600)
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_seq_parallel_two_gpus_matches_one_gpu(gla):
+@pytest.mark.parametrize("use_exchange", [False, True], ids=["torch-all-gather", "c-abi-nccl-exchange"])
+def test_seq_parallel_two_gpus_matches_one_gpu(gla, use_exchange):
     world = 2
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, out)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, out, use_exchange)) for r in range(world)]
     for pr in procs:
         pr.start()
     for pr in procs:
