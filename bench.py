@@ -65,6 +65,9 @@ def kernel_work(name, K, V, BT=128):
         "tc_out": (2 * K * V + 2 * BT * V, 2 * K + 2 * BT + st + 2 * V + 2 * V),
         "tc_scan_bwd": (2 * K * V, 2 * K + 2 * V + st),
         "tc_out_dv": (2 * K * V + 2 * BT * V, 2 * K + 2 * BT + st + 2 * V + 2 * V),
+        # state scan fused with the output GEMM: scan-side x, y, state store, output-side x, A, output
+        "tc_scan_out": (4 * K * V + 2 * BT * V, 4 * K + 2 * BT + 4 * V + st),
+        "tc_scan_out_bwd": (4 * K * V + 2 * BT * V, 4 * K + 2 * BT + 4 * V + st),
         "tc_dqk": (2 * BT * V + 4 * K * V + 4 * BT * K,
                    2 * V + 2 * V + 2 * st + 2 * K + 2 * K + 4 * K + 2 * K + 2 * K + 4 * K),
         "recurrent_decode": (None, None),

@@ -26,6 +26,7 @@
 // swizzle that TMA writes and the UMMA descriptors describe.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -749,6 +750,339 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 }
 
 // ===========================================================================
+// k_scan_out: the state scan fused with the chunk-output GEMM.  grid (V/128, H, B*nspan)
+// (or (V/128, H, N) for a padded varlen problem), 384 threads, one CTA per SM.
+//   fwd: h_{c+1} = D_c h_c + kdec_c^T v_c;   o_c  = qhat_c h_c + A_c v_c
+//   bwd: dh_{c-1} = D_c dh_c + qhat_c^T do_c; dv_c = kdec_c dh_c + A_c^T do_c
+// The chunk-start state is read from TMEM once per chunk: its bf16 copy is written into
+// shared memory in the 128-byte-swizzled layout that is both the B operand of the output
+// GEMM and the source of the TMA store of the chunk states, so the output GEMM never
+// reads the states back from HBM (the separate k_out does).
+//   warp 0      TMA producer: per chunk the y tile (v or do; 2 slots) and a ring of
+//               32 KB stages: output-side x tiles (qhat / kdec), the A tiles, scan-side x tiles
+//   warp 1      MMA issuer: o = X h (K/64 x 4 MMAs) + A' Y (8), then the scan (8 per state half)
+//   warps 4-11  per chunk: wait for the chunk's MMAs, scale the state in TMEM by D and
+//               write its bf16 copy (the next chunk's operand), issue the state stores;
+//               then drain the previous chunk's output accumulator into its (now free)
+//               y slot and TMA-store it
+// TMEM: state [K rows as 128-lane halves x 128 columns] fp32 in columns [0, 256), two
+// output accumulators [128 tokens x 128] in [256, 384) and [384, 512).
+// ===========================================================================
+struct FusedMaps {
+  CUtensorMap sx;  // scan-side x: fwd kdec, bwd qhat; [B,T,H,K] box (64,1,128,1)
+  CUtensorMap y;   // fwd v, bwd do; [B,T,H,V] box (64,1,128,1)
+  CUtensorMap ox;  // output-side x: fwd qhat, bwd kdec; box (64,1,128,1)
+  CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1), bwd box (64,1,64,1)
+  CUtensorMap st;  // chunk states [B*NTb*H, K, V] bf16, box (64,32,1), 128-byte swizzle (store)
+  CUtensorMap o;   // output [B,T,H,V] box (64,1,128,1) (store)
+};
+
+constexpr int FO_THREADS = 384;
+constexpr uint32_t FO_STAGE = 2 * TILE_BYTES;  // 32 KB
+__host__ __device__ constexpr int fo_stages(int K) { return K == 256 ? 3 : 4; }
+static size_t fo_smem(int K) {
+  return (size_t)K * 256 + 2 * (size_t)FO_STAGE + (size_t)fo_stages(K) * FO_STAGE + 1024;
+}
+
+template <bool SEG>
+__global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constant__ FusedMaps maps, ScanParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nh = p.K / 128;      // state halves
+  const int nxs = p.K / 128;     // output-side x stages per chunk (two 64-column tiles each)
+  const int S = fo_stages(p.K);  // ring stages
+  const uint32_t half_bytes = (uint32_t)p.K * 128;  // one 64-column half of the bf16 state copy
+  unsigned char* hs = smem;                         // bf16 state copy: 2 halves [K rows][64 cols]
+  unsigned char* yslot0 = smem + 2 * half_bytes;    // 2 slots x [128 rows][128 cols] (two 16 KB tiles)
+  unsigned char* ring = yslot0 + 2 * FO_STAGE;
+  __shared__ __align__(8) uint64_t full[4], empty[4], y_full[2], y_empty[2], acc_empty[2], bar_pass, bar_chunk,
+      bar_done;
+  __shared__ uint32_t tmem_base;
+
+  const int vt = blockIdx.x, h = blockIdx.y;
+  const int b = SEG ? 0 : blockIdx.z / p.nspan, sp_ = SEG ? 0 : blockIdx.z % p.nspan;
+  const int sq = SEG ? (int)blockIdx.z : b;
+  const int v0 = vt * BV;
+  const int i0 = SEG ? p.blk_off[blockIdx.z] : sp_ * p.span_len;
+  const int n_it = SEG ? p.blk_off[blockIdx.z + 1] - i0 : min(p.span_len, p.NTb - i0);
+  const size_t span_off = (size_t)sp_ * p.B * p.H * p.K * p.V;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (warp == 0) {
+    ptx::tmem_alloc(&tmem_base, 512);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 32) {
+    for (int s = 0; s < 4; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&y_full[s], 1);
+      ptx::mbar_init(&y_empty[s], 2);    // the two output-half leaders, after their stores read the slot
+      ptx::mbar_init(&acc_empty[s], 8);  // the eight epilogue warps, after their TMEM reads
+    }
+    ptx::mbar_init(&bar_pass, 8);
+    ptx::mbar_init(&bar_chunk, 1);
+    ptx::mbar_init(&bar_done, 1);
+    ptx::fence_mbar_init();
+  }
+  auto chunk_of = [&](int i) {
+    if constexpr (SEG) return p.reverse ? i0 + n_it - 1 - i : i0 + i;
+    else return p.reverse ? p.NTb - 1 - (i0 + i) : i0 + i;
+  };
+  auto yslot = [&](int i) { return yslot0 + (i & 1) * FO_STAGE; };
+  auto oacc = [&](int i) { return tmem_base + 256u + (uint32_t)((i & 1) * 128); };
+
+  // pass warps: state half hf, TMEM lane quadrant qd
+  const int pw = warp - 4;
+  const int hf = pw >> 2, qd = warp & 3;
+  const int krow = hf * 128 + qd * 32 + lane;
+  const bool pass_warp = warp >= 4;
+  const bool active = pass_warp && hf < nh;
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (active) {  // initial state -> TMEM
+    const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0;
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      float r[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[span_off + srow + cb * 32 + j] : 0.f;
+      ptx::tmem_st32(tmem_lane_addr(tmem_base, qd * 32, hf * 128 + cb * 32), r);
+    }
+    ptx::tmem_st_wait();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      uint32_t n = 0;
+      int ny = 0;  // y tiles armed
+      bool ok = true;
+      for (int i = 0; i < n_it && ok; ++i) {
+        const int c = chunk_of(i), row0 = c * BT;
+        const int nst = nxs + 1 + nh;
+        for (int e = 0; e < nst && ok; ++e, ++n) {
+          if (e == nxs) {  // the y tile is first needed with the A stage; its slot frees late
+            ok = ptx::mbar_wait(&y_empty[i & 1], (uint32_t)(((i >> 1) & 1) ^ 1));
+            if (!ok) break;
+            ptx::mbar_arrive_expect_tx(&y_full[i & 1], FO_STAGE);
+            ptx::tma_load_4d(yslot(i), &maps.y, v0, h, row0, b, &y_full[i & 1]);
+            ptx::tma_load_4d(yslot(i) + TILE_BYTES, &maps.y, v0 + 64, h, row0, b, &y_full[i & 1]);
+            ++ny;
+          }
+          const int s = (int)(n % (uint32_t)S);
+          ok = ptx::mbar_wait(&empty[s], ((n / S) & 1) ^ 1);
+          if (!ok) break;
+          unsigned char* st = ring + s * FO_STAGE;
+          ptx::mbar_arrive_expect_tx(&full[s], FO_STAGE);
+          if (e < nxs) {  // output-side x: 64-column tiles 2e, 2e+1
+            ptx::tma_load_4d(st, &maps.ox, (2 * e) * 64, h, row0, b, &full[s]);
+            ptx::tma_load_4d(st + TILE_BYTES, &maps.ox, (2 * e + 1) * 64, h, row0, b, &full[s]);
+          } else if (e == nxs) {  // A: two 64-token blocks
+            for (int j = 0; j < 2; ++j) {
+              if (!p.reverse) {
+                ptx::tma_load_4d(st + j * TILE_BYTES, &maps.a, j * 64, h, row0, b, &full[s]);
+              } else {
+                ptx::tma_load_4d(st + j * TILE_BYTES, &maps.a, 0, h, row0 + j * 64, b, &full[s]);
+                ptx::tma_load_4d(st + j * TILE_BYTES + TILE_BYTES / 2, &maps.a, 64, h, row0 + j * 64, b, &full[s]);
+              }
+            }
+          } else {  // scan-side x: the two 64-column tiles of state half (e - nxs - 1)
+            const int half = e - nxs - 1;
+            ptx::tma_load_4d(st, &maps.sx, half * 128, h, row0, b, &full[s]);
+            ptx::tma_load_4d(st + TILE_BYTES, &maps.sx, half * 128 + 64, h, row0, b, &full[s]);
+          }
+        }
+      }
+      // loads still in flight after an early exit land before the CTA leaves: wait for the
+      // last armed phase of every stage and y slot
+      const uint32_t armed = n;
+      for (uint32_t m = armed > (uint32_t)S ? armed - S : 0; m < armed; ++m)
+        ptx::mbar_wait(&full[m % S], (m / S) & 1);
+      for (int m = ny > 2 ? ny - 2 : 0; m < ny; ++m) ptx::mbar_wait(&y_full[m & 1], (uint32_t)((m >> 1) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      uint32_t n = 0;
+      bool ok = true, any = false;
+      const uint32_t ID_K = ptx::idesc_bf16(128, 128, false, true);
+      const uint32_t ID_M = ptx::idesc_bf16(128, 128, true, true);
+      for (int i = 0; i < n_it && ok; ++i) {
+        ok = ptx::mbar_wait(&bar_pass, (uint32_t)(i & 1)) &&
+             ptx::mbar_wait(&acc_empty[i & 1], (uint32_t)(((i >> 1) & 1) ^ 1)) &&
+             ptx::mbar_wait(&y_full[i & 1], (uint32_t)((i >> 1) & 1));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        any = true;
+        const uint32_t dacc = oacc(i);
+        const unsigned char* ys = yslot(i);
+        // output, part 1: X[128 x K] (K-major tiles) x h_c[K x 128] (bf16 copy, MN-major)
+        for (int e = 0; e < nxs && ok; ++e, ++n) {
+          const int s = (int)(n % (uint32_t)S);
+          ok = ptx::mbar_wait(&full[s], (n / S) & 1);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const unsigned char* st = ring + s * FO_STAGE;
+          for (int t = 0; t < 2; ++t) {
+            const int kb = 2 * e + t;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              ptx::mma_bf16_ss(dacc, desc_kmajor(st + t * TILE_BYTES, ks * 32),
+                               desc_mnmajor(hs, (uint32_t)(kb * 64 + ks * 16) * 128, half_bytes), ID_K,
+                               (kb | ks) ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        // output, part 2: A' [128 x 128] x Y [128 x 128]
+        {
+          const int s = (int)(n % (uint32_t)S);
+          ok = ptx::mbar_wait(&full[s], (n / S) & 1);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const unsigned char* st = ring + s * FO_STAGE;
+          for (int j = 0; j < 2; ++j) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = p.reverse ? desc_mnmajor(st + j * TILE_BYTES, ks * 2048, TILE_BYTES / 2)
+                                            : desc_kmajor(st + j * TILE_BYTES, ks * 32);
+              ptx::mma_bf16_ss(dacc, ad, desc_mnmajor(ys, (uint32_t)(j * 64 + ks * 16) * 128, TILE_BYTES),
+                               p.reverse ? ID_M : ID_K, 1u);
+            }
+          }
+          ptx::mma_commit(&empty[s]);
+          ++n;
+        }
+        // state scan: state[half] += X_half^T Y (X M-major, Y N-major, contraction over tokens)
+        for (int half = 0; half < nh && ok; ++half, ++n) {
+          const int s = (int)(n % (uint32_t)S);
+          ok = ptx::mbar_wait(&full[s], (n / S) & 1);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const unsigned char* st = ring + s * FO_STAGE;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            ptx::mma_bf16_ss(tmem_base + half * 128, desc_mnmajor(st, ks * 2048, TILE_BYTES),
+                             desc_mnmajor(ys, ks * 2048, TILE_BYTES), ID_M, 1u);
+          ptx::mma_commit(&empty[s]);
+        }
+        if (ok) ptx::mma_commit(&bar_chunk);  // state, output accumulator, y slot and state copy are done
+      }
+      if (any) {  // every issued MMA has completed before TMEM is released
+        ptx::mma_commit(&bar_done);
+        ptx::mbar_wait(&bar_done, 0);
+      }
+    }
+  } else if (pass_warp) {
+    const int rbase_h = h;  // state-row index: (b * NTb + c) * H + h
+    // epilogue of chunk j: output accumulator -> bf16 -> y slot of chunk j -> TMA store
+    auto epilogue = [&](int j) {
+      const int c = chunk_of(j);
+      unsigned char* tile = yslot(j) + hf * TILE_BYTES;  // output columns hf*64 .. +63
+      const int t = qd * 32 + lane;                      // token row of this thread
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        float r[32];
+        ptx::tmem_ld32(tmem_lane_addr(oacc(j), qd * 32, hf * 64 + cb * 32), r);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int j8 = 0; j8 < 4; ++j8)
+          *reinterpret_cast<uint4*>(tile + ptx::sw128(t, cb * 64 + j8 * 16)) =
+              make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
+                         ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&acc_empty[j & 1]);
+      ptx::fence_async_smem();
+      asm volatile("bar.sync %0, 128;" ::"r"(2 + hf) : "memory");
+      if (qd == 0 && lane == 0) {  // rows past T are clipped by the tensor map
+        ptx::tma_store_4d(&maps.o, v0 + hf * 64, h, c * BT, b, tile);
+        ptx::bulk_commit();
+        ptx::bulk_wait_read<0>();
+        ptx::mbar_arrive(&y_empty[j & 1]);
+      }
+    };
+    auto decay_of = [&](int i) {
+      return active && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
+    };
+    bool ok = true;
+    float d_next = decay_of(0);
+    for (int i = 0; i < n_it; ++i) {
+      const int c = chunk_of(i);
+      const float d = d_next;
+      d_next = decay_of(i + 1);
+      if (i > 0) {
+        ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_chunk, (uint32_t)((i - 1) & 1)));
+        ptx::tc_fence_after();
+        if (!ok) break;
+      }
+      if (active) {
+        if (lane == 0) ptx::bulk_wait_read<0>();  // this warp's previous state store has read the copy
+        __syncwarp();
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+          float r[32];
+          const uint32_t ta = tmem_lane_addr(tmem_base, qd * 32, hf * 128 + cb * 32);
+          ptx::tmem_ld32(ta, r);
+          ptx::tmem_ld_wait();
+          unsigned char* dst = hs + (cb >> 1) * half_bytes;
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8)
+            *reinterpret_cast<uint4*>(dst + ptx::sw128(krow, (cb & 1) * 64 + j8 * 16)) =
+                make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
+                           ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] *= d;
+          ptx::tmem_st32(ta, r);
+        }
+        ptx::tmem_st_wait();
+      }
+      ptx::fence_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (active && p.states) {
+          const int rrow = (b * p.NTb + c) * p.H + rbase_h;
+          const int k0 = hf * 128 + qd * 32;
+          ptx::tma_store_3d(&maps.st, v0, k0, rrow, hs + (uint32_t)k0 * 128);
+          ptx::tma_store_3d(&maps.st, v0 + 64, k0, rrow, hs + half_bytes + (uint32_t)k0 * 128);
+          ptx::bulk_commit();
+        }
+        ptx::mbar_arrive(&bar_pass);
+      }
+      if (i > 0) epilogue(i - 1);
+    }
+    if (ok && n_it > 0) {
+      ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_chunk, (uint32_t)((n_it - 1) & 1)));
+      ptx::tc_fence_after();
+      if (ok) epilogue(n_it - 1);
+    }
+    if (ok && active && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
+      const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        float r[32];
+        ptx::tmem_ld32(tmem_lane_addr(tmem_base, qd * 32, hf * 128 + cb * 32), r);
+        ptx::tmem_ld_wait();
+        float4* dst = reinterpret_cast<float4*>(p.fin + srow + cb * 32);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) dst[j4] = make_float4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
+      }
+    }
+    if (lane == 0) ptx::bulk_wait<0>();  // this warp's stores are complete
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tmem_base, 512);
+}
+
+// ===========================================================================
 // k_dqk: dq, dk, dg of one (batch, chunk, head, 64-wide K tile).  grid (K/64, NTb, B*H),
 // 256 threads, two CTAs per SM (256 TMEM columns and ~100 KB shared memory each), so one
 // CTA's epilogue runs while the other streams its operands.
@@ -1351,24 +1685,35 @@ static cudaError_t set_smem(KernelT k, size_t bytes) {
 }
 
 // One state scan (forward h or reverse dh), split into spans when that fills the GPU.
+// With `fm`, the pass that stores the chunk states is k_scan_out, which also writes the
+// chunk outputs (fwd o, bwd dv) through fm->o.
 static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, const float* D, const float* init,
                     float* fin, bf16* states, const SpanBufs& sb, Spans spn, cudaStream_t st, const char* name,
-                    const int* blk_off = nullptr) {
+                    const int* blk_off = nullptr, const FusedMaps* fm = nullptr) {
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  if (fm && (e = set_smem(k_scan_out<false>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
   if (blk_off != nullptr) {  // padded varlen problem: one CTA column per segment
-    if ((e = set_smem(k_scan<true>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, blk_off};
-    k_scan<true><<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
+    if (fm) {
+      if ((e = set_smem(k_scan_out<true>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
+      k_scan_out<true><<<dim3(s.V / BV, s.H, s.N), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+    } else {
+      if ((e = set_smem(k_scan<true>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+      k_scan<true><<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
+    }
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
   if (spn.n <= 1) {
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, nullptr};
-    k_scan<false><<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+    if (fm)
+      k_scan_out<false><<<dim3(s.V / BV, s.H, s.B), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+    else
+      k_scan<false><<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
@@ -1387,10 +1732,23 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
   {
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
-    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    if (fm)
+      k_scan_out<false><<<dim3(s.V / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+    else
+      k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
   }
   return TOPS_OK;
+}
+
+// The fused scan + output kernel is the default; TOPS_GLA_UNFUSED_OUT=1 selects the
+// separate state scan and k_out GEMM (same results; kept for comparison).
+static bool fused_out() {
+  static const bool on = [] {
+    const char* e = getenv("TOPS_GLA_UNFUSED_OUT");
+    return !(e && e[0] == '1');
+  }();
+  return on;
 }
 
 // Forward of a fixed-length (or padded varlen, blk_off != null) problem: o, ht and (in
@@ -1412,11 +1770,20 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   okm = okm && map_tok(&sm.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
         map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_state_store(&sm.st, sv.h, s.B * NTb * s.H, s.K, s.V);
   OutMaps om;
-  if (o != nullptr)
+  FusedMaps fm;
+  const bool fused = o != nullptr && fused_out();
+  if (o != nullptr && !fused)
     okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
           map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) &&
           map_tok(&om.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  if (fused)
+    okm = okm && map_tok(&fm.sx, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_tok(&fm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+          map_tok(&fm.ox, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) &&
+          map_state(&fm.st, sv.h, s.B * NTb * s.H, s.K, s.V, 32) &&
+          map_tok(&fm.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   {
@@ -1428,9 +1795,10 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
     TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   }
-  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, "tc_scan", blk_off);
+  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, fused ? "tc_scan_out" : "tc_scan",
+                    blk_off, fused ? &fm : nullptr);
   if (rc) return rc;
-  if (o == nullptr) return TOPS_OK;  // final state only
+  if (o == nullptr || fused) return TOPS_OK;  // final state only, or o written by the fused scan
   {
     LaunchTimer lt(st, "tc_out");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 0, static_cast<bf16*>(o)};
@@ -1485,9 +1853,20 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     return run_scan(s, sm, 1, sv.D, dht, dh0, nullptr, sb, spn, st, "tc_scan_bwd", blk_off);
   }
   OutMaps om;
-  okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) && map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
-        map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  FusedMaps fm;
+  const bool fused = fused_out();
+  if (fused)
+    okm = okm && map_tok(&fm.sx, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_tok(&fm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+          map_tok(&fm.ox, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
+          map_state(&fm.st, dhs, s.B * NTb * s.H, s.K, s.V, 32) &&
+          map_tok(&fm.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+  else
+    okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+          map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
+          map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
+          map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   DqkMaps dm;
   okm = okm && map_tok(&dm.dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
         map_tok(&dm.v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
@@ -1498,8 +1877,10 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
         map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
-  if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, "tc_scan_bwd", blk_off))) return rc;
-  {
+  if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, fused ? "tc_scan_out_bwd" : "tc_scan_bwd", blk_off,
+                     fused ? &fm : nullptr)))
+    return rc;
+  if (!fused) {
     LaunchTimer lt(st, "tc_out_dv");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 1, static_cast<bf16*>(dv)};
     if ((e = set_smem(k_out, out_smem())) != cudaSuccess) return cuda_status(e, "tc out attr");
