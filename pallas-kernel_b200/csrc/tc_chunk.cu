@@ -755,16 +755,19 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 //   fwd: h_{c+1} = D_c h_c + kdec_c^T v_c;   o_c  = qhat_c h_c + A_c v_c
 //   bwd: dh_{c-1} = D_c dh_c + qhat_c^T do_c; dv_c = kdec_c dh_c + A_c^T do_c
 // The chunk-start state is read from TMEM once per chunk: its bf16 copy is written into
-// shared memory in the 128-byte-swizzled layout that is both the B operand of the output
-// GEMM and the source of the TMA store of the chunk states, so the output GEMM never
-// reads the states back from HBM (the separate k_out does).
+// shared memory in the 128-byte-swizzled layout of the B operand of the output GEMM, so
+// the output GEMM never reads the states back from HBM (the separate k_out does).  The
+// copy and the output tiles go to HBM through ordinary coalesced stores (whole rows per
+// warp instruction), not through the TMA unit, whose per-SM throughput (about 84 GB/s)
+// the operand loads (224 KB per chunk at K = 256) already need.
 //   warp 0      TMA producer: per chunk the y tile (v or do; 2 slots) and a ring of
-//               32 KB stages: output-side x tiles (qhat / kdec), the A tiles, scan-side x tiles
-//   warp 1      MMA issuer: o = X h (K/64 x 4 MMAs) + A' Y (8), then the scan (8 per state half)
+//               32 KB stages: the A tiles, output-side x tiles (qhat / kdec), scan-side x tiles
+//   warp 1      MMA issuer: o = A' Y (8 MMAs; needs no state, so it overlaps the state pass),
+//               then o += X h (K/64 x 4) and the scan (8 per state half)
 //   warps 4-11  per chunk: wait for the chunk's MMAs, scale the state in TMEM by D and
-//               write its bf16 copy (the next chunk's operand), issue the state stores;
+//               write its bf16 copy (the next chunk's operand), store the copy's rows;
 //               then drain the previous chunk's output accumulator into its (now free)
-//               y slot and TMA-store it
+//               y slot and store it
 // TMEM: state [K rows as 128-lane halves x 128 columns] fp32 in columns [0, 256), two
 // output accumulators [128 tokens x 128] in [256, 384) and [384, 512).
 // ===========================================================================
@@ -773,8 +776,7 @@ struct FusedMaps {
   CUtensorMap y;   // fwd v, bwd do; [B,T,H,V] box (64,1,128,1)
   CUtensorMap ox;  // output-side x: fwd qhat, bwd kdec; box (64,1,128,1)
   CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1), bwd box (64,1,64,1)
-  CUtensorMap st;  // chunk states [B*NTb*H, K, V] bf16, box (64,32,1), 128-byte swizzle (store)
-  CUtensorMap o;   // output [B,T,H,V] box (64,1,128,1) (store)
+  bf16* out;       // output [B, T, H, V] bf16 (fwd o, bwd dv)
 };
 
 constexpr int FO_THREADS = 384;
@@ -819,7 +821,7 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
     }
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&y_full[s], 1);
-      ptx::mbar_init(&y_empty[s], 2);    // the two output-half leaders, after their stores read the slot
+      ptx::mbar_init(&y_empty[s], 8);    // the eight epilogue warps, after they read their output rows
       ptx::mbar_init(&acc_empty[s], 8);  // the eight epilogue warps, after their TMEM reads
     }
     ptx::mbar_init(&bar_pass, 8);
@@ -867,7 +869,7 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         const int c = chunk_of(i), row0 = c * BT;
         const int nst = nxs + 1 + nh;
         for (int e = 0; e < nst && ok; ++e, ++n) {
-          if (e == nxs) {  // the y tile is first needed with the A stage; its slot frees late
+          if (e == 0) {  // the y tile is first needed with the A stage
             ok = ptx::mbar_wait(&y_empty[i & 1], (uint32_t)(((i >> 1) & 1) ^ 1));
             if (!ok) break;
             ptx::mbar_arrive_expect_tx(&y_full[i & 1], FO_STAGE);
@@ -880,10 +882,10 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
           if (!ok) break;
           unsigned char* st = ring + s * FO_STAGE;
           ptx::mbar_arrive_expect_tx(&full[s], FO_STAGE);
-          if (e < nxs) {  // output-side x: 64-column tiles 2e, 2e+1
-            ptx::tma_load_4d(st, &maps.ox, (2 * e) * 64, h, row0, b, &full[s]);
-            ptx::tma_load_4d(st + TILE_BYTES, &maps.ox, (2 * e + 1) * 64, h, row0, b, &full[s]);
-          } else if (e == nxs) {  // A: two 64-token blocks
+          if (e >= 1 && e <= nxs) {  // output-side x: 64-column tiles 2x, 2x+1, x = e - 1
+            ptx::tma_load_4d(st, &maps.ox, (2 * (e - 1)) * 64, h, row0, b, &full[s]);
+            ptx::tma_load_4d(st + TILE_BYTES, &maps.ox, (2 * (e - 1) + 1) * 64, h, row0, b, &full[s]);
+          } else if (e == 0) {  // A: two 64-token blocks
             for (int j = 0; j < 2; ++j) {
               if (!p.reverse) {
                 ptx::tma_load_4d(st + j * TILE_BYTES, &maps.a, j * 64, h, row0, b, &full[s]);
@@ -913,33 +915,14 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       const uint32_t ID_K = ptx::idesc_bf16(128, 128, false, true);
       const uint32_t ID_M = ptx::idesc_bf16(128, 128, true, true);
       for (int i = 0; i < n_it && ok; ++i) {
-        ok = ptx::mbar_wait(&bar_pass, (uint32_t)(i & 1)) &&
-             ptx::mbar_wait(&acc_empty[i & 1], (uint32_t)(((i >> 1) & 1) ^ 1)) &&
+        // o = A' Y does not need the state: it runs while the pass warps prepare chunk i
+        ok = ptx::mbar_wait(&acc_empty[i & 1], (uint32_t)(((i >> 1) & 1) ^ 1)) &&
              ptx::mbar_wait(&y_full[i & 1], (uint32_t)((i >> 1) & 1));
         if (!ok) break;
         ptx::tc_fence_after();
         any = true;
         const uint32_t dacc = oacc(i);
         const unsigned char* ys = yslot(i);
-        // output, part 1: X[128 x K] (K-major tiles) x h_c[K x 128] (bf16 copy, MN-major)
-        for (int e = 0; e < nxs && ok; ++e, ++n) {
-          const int s = (int)(n % (uint32_t)S);
-          ok = ptx::mbar_wait(&full[s], (n / S) & 1);
-          if (!ok) break;
-          ptx::tc_fence_after();
-          const unsigned char* st = ring + s * FO_STAGE;
-          for (int t = 0; t < 2; ++t) {
-            const int kb = 2 * e + t;
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              ptx::mma_bf16_ss(dacc, desc_kmajor(st + t * TILE_BYTES, ks * 32),
-                               desc_mnmajor(hs, (uint32_t)(kb * 64 + ks * 16) * 128, half_bytes), ID_K,
-                               (kb | ks) ? 1u : 0u);
-          }
-          ptx::mma_commit(&empty[s]);
-        }
-        if (!ok) break;
-        // output, part 2: A' [128 x 128] x Y [128 x 128]
         {
           const int s = (int)(n % (uint32_t)S);
           ok = ptx::mbar_wait(&full[s], (n / S) & 1);
@@ -952,12 +935,32 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
               const uint64_t ad = p.reverse ? desc_mnmajor(st + j * TILE_BYTES, ks * 2048, TILE_BYTES / 2)
                                             : desc_kmajor(st + j * TILE_BYTES, ks * 32);
               ptx::mma_bf16_ss(dacc, ad, desc_mnmajor(ys, (uint32_t)(j * 64 + ks * 16) * 128, TILE_BYTES),
-                               p.reverse ? ID_M : ID_K, 1u);
+                               p.reverse ? ID_M : ID_K, (j | ks) ? 1u : 0u);
             }
           }
           ptx::mma_commit(&empty[s]);
           ++n;
         }
+        ok = ptx::mbar_wait(&bar_pass, (uint32_t)(i & 1));  // scaled state and its bf16 copy are ready
+        if (!ok) break;
+        ptx::tc_fence_after();
+        // o += X[128 x K] (K-major tiles) x h_c[K x 128] (bf16 copy, MN-major)
+        for (int e = 0; e < nxs && ok; ++e, ++n) {
+          const int s = (int)(n % (uint32_t)S);
+          ok = ptx::mbar_wait(&full[s], (n / S) & 1);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const unsigned char* st = ring + s * FO_STAGE;
+          for (int t = 0; t < 2; ++t) {
+            const int kb = 2 * e + t;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              ptx::mma_bf16_ss(dacc, desc_kmajor(st + t * TILE_BYTES, ks * 32),
+                               desc_mnmajor(hs, (uint32_t)(kb * 64 + ks * 16) * 128, half_bytes), ID_K, 1u);
+          }
+          ptx::mma_commit(&empty[s]);
+        }
+        if (!ok) break;
         // state scan: state[half] += X_half^T Y (X M-major, Y N-major, contraction over tokens)
         for (int half = 0; half < nh && ok; ++half, ++n) {
           const int s = (int)(n % (uint32_t)S);
@@ -979,8 +982,10 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       }
     }
   } else if (pass_warp) {
-    const int rbase_h = h;  // state-row index: (b * NTb + c) * H + h
-    // epilogue of chunk j: output accumulator -> bf16 -> y slot of chunk j -> TMA store
+    // epilogue of chunk j: output accumulator -> bf16 -> y slot of chunk j -> HBM.  Warp
+    // (hf, qd) owns output rows qd*32 .. +31, columns hf*64 .. +63: it writes them into the
+    // slot from TMEM (a row per lane) and reads them back four rows of 128 bytes per
+    // instruction for coalesced stores.
     auto epilogue = [&](int j) {
       const int c = chunk_of(j);
       unsigned char* tile = yslot(j) + hf * TILE_BYTES;  // output columns hf*64 .. +63
@@ -999,14 +1004,17 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&acc_empty[j & 1]);
-      ptx::fence_async_smem();
-      asm volatile("bar.sync %0, 128;" ::"r"(2 + hf) : "memory");
-      if (qd == 0 && lane == 0) {  // rows past T are clipped by the tensor map
-        ptx::tma_store_4d(&maps.o, v0 + hf * 64, h, c * BT, b, tile);
-        ptx::bulk_commit();
-        ptx::bulk_wait_read<0>();
-        ptx::mbar_arrive(&y_empty[j & 1]);
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = qd * 32 + 4 * it + (lane >> 3), row = c * BT + rr;
+        const uint4 x = *reinterpret_cast<const uint4*>(tile + ptx::sw128(rr, (lane & 7) * 16));
+        if (row < p.T)
+          *reinterpret_cast<uint4*>(maps.out + (((size_t)b * p.T + row) * p.H + h) * p.V + v0 + hf * 64 +
+                                    (lane & 7) * 8) = x;
       }
+      ptx::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&y_empty[j & 1]);
     };
     auto decay_of = [&](int i) {
       return active && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
@@ -1023,8 +1031,6 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         if (!ok) break;
       }
       if (active) {
-        if (lane == 0) ptx::bulk_wait_read<0>();  // this warp's previous state store has read the copy
-        __syncwarp();
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
           float r[32];
@@ -1046,15 +1052,16 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       ptx::fence_async_smem();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        if (active && p.states) {
-          const int rrow = (b * p.NTb + c) * p.H + rbase_h;
-          const int k0 = hf * 128 + qd * 32;
-          ptx::tma_store_3d(&maps.st, v0, k0, rrow, hs + (uint32_t)k0 * 128);
-          ptx::tma_store_3d(&maps.st, v0 + 64, k0, rrow, hs + half_bytes + (uint32_t)k0 * 128);
-          ptx::bulk_commit();
+      if (lane == 0) ptx::mbar_arrive(&bar_pass);
+      if (active && p.states) {  // this warp's 32 state rows, two rows (2 x 256 B) per instruction
+        const size_t rbase = ((size_t)(b * p.NTb + c) * p.H + h) * p.K;
+        const int hb = (lane >> 3) & 1, c16 = lane & 7;
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int r = hf * 128 + qd * 32 + 2 * it + (lane >> 4);
+          const uint4 x = *reinterpret_cast<const uint4*>(hs + hb * half_bytes + ptx::sw128(r, c16 * 16));
+          *reinterpret_cast<uint4*>(p.states + (rbase + r) * p.V + v0 + hb * 64 + c16 * 8) = x;
         }
-        ptx::mbar_arrive(&bar_pass);
       }
       if (i > 0) epilogue(i - 1);
     }
@@ -1075,7 +1082,6 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         for (int j4 = 0; j4 < 8; ++j4) dst[j4] = make_float4(r[4 * j4], r[4 * j4 + 1], r[4 * j4 + 2], r[4 * j4 + 3]);
       }
     }
-    if (lane == 0) ptx::bulk_wait<0>();  // this warp's stores are complete
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -1781,9 +1787,8 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     okm = okm && map_tok(&fm.sx, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_tok(&fm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
           map_tok(&fm.ox, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) &&
-          map_state(&fm.st, sv.h, s.B * NTb * s.H, s.K, s.V, 32) &&
-          map_tok(&fm.o, o, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
+  fm.out = static_cast<bf16*>(o);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   {
@@ -1855,13 +1860,12 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   OutMaps om;
   FusedMaps fm;
   const bool fused = fused_out();
+  fm.out = static_cast<bf16*>(dv);
   if (fused)
     okm = okm && map_tok(&fm.sx, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_tok(&fm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
           map_tok(&fm.ox, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
-          map_state(&fm.st, dhs, s.B * NTb * s.H, s.K, s.V, 32) &&
-          map_tok(&fm.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
+          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64);
   else
     okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
