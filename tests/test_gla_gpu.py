@@ -583,3 +583,55 @@ def test_pinned_pipeline_back_to_back_steps(gla):
                                False, block=sv.get("block"))
         for nm, a, b in zip(("dq", "dk", "dv", "dg"), o, want[:4]):
             assert_rel_l2(nm, a.float(), b.float().cpu(), 1e-3)
+
+
+_UNFUSED_CHILD = r"""
+import sys
+import numpy as np
+import torch
+root = sys.argv[1]
+sys.path[:0] = [root, root + "/pallas-kernel_b200", root + "/tests", root + "/tests/golden"]
+import cases as GC
+from oracle import gla_oracle as O
+from tops import _C
+from tops.ops.gla import _core
+B, T, H, K, V = 1, 333, 3, 128, 256
+rng = np.random.default_rng(42)
+q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+do = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+h0 = rng.standard_normal((B, H, K, V), dtype=np.float32)
+dev = lambda x, dt=torch.float32: torch.from_numpy(np.ascontiguousarray(x)).to("cuda", dt)
+bf = torch.bfloat16
+p = _core.make_plan(dev(q, bf), V, 64, None, K ** -0.5)
+_C.timing_enable(True)
+o, ht, sv = _core.chunk_fwd(p, dev(q, bf), dev(k, bf), dev(v, bf), dev(g), dev(h0), True, save=True)
+dq, dk, dv, dg, dh0 = _core.chunk_bwd(p, dev(q, bf), dev(k, bf), dev(v, bf), dev(g), dev(h0), dev(do, bf), None,
+                                      sv.get("g_cumsum"), sv.get("A"), sv.get("h"), True, block=sv.get("block"))
+torch.cuda.synchronize()
+_C.timing_enable(False)
+names = {n for n, _ in _C.timing_collect()}
+assert {"tc_scan", "tc_out", "tc_scan_bwd", "tc_out_dv"} <= names, names
+o_r, ht_r = O.chunk_gla(q, k, v, g, initial_state=h0, output_final_state=True, chunk_size=64)
+ref = O.chunk_gla_bwd(q, k, v, g, None, K ** -0.5, h0, None, None, do, None, None, 64)
+rel = lambda a, b: float(np.linalg.norm(a.float().cpu().numpy() - b) / np.linalg.norm(b))
+errs = [rel(a, b) for a, b in zip((o, ht, dq, dk, dv, dg, dh0), (o_r, ht_r) + tuple(ref))]
+assert max(errs) < 2e-2, errs
+assert _C.lib().tops_gla_device_error() == 0
+print("UNFUSED_OK", max(errs))
+"""
+
+
+def test_unfused_scan_and_output_path(gla):
+    """TOPS_GLA_UNFUSED_OUT=1 selects the separate state scan and k_out GEMM (read once per
+    process, so it runs in a child): same results as the oracle, and those kernels ran."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = str(Path(__file__).resolve().parents[1])
+    env = dict(os.environ, TOPS_GLA_UNFUSED_OUT="1")
+    r = subprocess.run([sys.executable, "-c", _UNFUSED_CHILD, root], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "UNFUSED_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
