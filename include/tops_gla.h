@@ -94,6 +94,11 @@ TOPS_API int32_t tops_gla_abi_version(void);
 /* First error code recorded by a device-side bounded wait since the last call
  * (0 = none, 1 = an mbarrier wait timed out); reading clears it.  Synchronizes. */
 TOPS_API int32_t tops_gla_device_error(void);
+/* Check of the failure path: launches one thread that waits on an mbarrier nothing will
+ * complete, so its bounded wait runs out (about 2 s) and records code 1 for
+ * tops_gla_device_error(); the kernel then returns and the context stays usable.
+ * Returns the launch status. */
+TOPS_API int tops_gla_selftest_wait_timeout(void* stream);
 /* 1 when the current device can run the tcgen05 (sm_100a) kernels. */
 TOPS_API int32_t tops_gla_has_tcgen05(void);
 

@@ -123,6 +123,7 @@ size_t fwd_workspace(const tops_gla_shape& s, bool own_saved);
 int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
         void* o, float* ht, void* saved, void* workspace, cudaStream_t st);
 int read_device_error();
+int selftest_wait_timeout(cudaStream_t st);
 size_t bwd_workspace(const tops_gla_shape& s, bool have_saved);
 int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
         const void* dO, const float* dht, const void* saved, void* dq, void* dk, void* dv, float* dg, float* dh0,
@@ -308,6 +309,10 @@ int32_t tops_gla_device_error(void) {
   int32_t e = decode::read_device_error();
   const int32_t e2 = tc::read_device_error();
   return e != 0 ? e : e2;
+}
+
+int tops_gla_selftest_wait_timeout(void* stream) {
+  return tc::selftest_wait_timeout(static_cast<cudaStream_t>(stream));
 }
 
 size_t tops_gla_chunk_saved_size(const tops_gla_shape* s) {

@@ -1512,6 +1512,23 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
 
 TOPS_DEVICE_ERROR_READER(read_device_error)
 
+// one thread waits on an mbarrier that nothing arrives on: the bounded wait gives up,
+// records DEVERR_MBAR_TIMEOUT and the kernel returns (the failure path, exercised on purpose)
+__global__ void k_wait_selftest() {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+    ptx::mbar_wait(&bar, 0);
+  }
+}
+
+int selftest_wait_timeout(cudaStream_t st) {
+  k_wait_selftest<<<1, 32, 0, st>>>();
+  TOPS_CUDA_LAUNCH_CHECK("wait_selftest");
+  return TOPS_OK;
+}
+
 // ---------------------------------------------------------------------------
 // host orchestration
 // ---------------------------------------------------------------------------

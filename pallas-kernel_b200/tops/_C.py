@@ -84,6 +84,7 @@ SIGNATURES = {
     "tops_gla_timing_collect": (I32, [C.c_char_p, I32, C.POINTER(C.c_float), I32]),
     "tops_gla_has_tcgen05": (I32, []),
     "tops_gla_device_error": (I32, []),
+    "tops_gla_selftest_wait_timeout": (C.c_int, [VP]),
     "tops_gla_num_chunks": (I32, [I32, I32, I32, VP, I32, VP]),
     "tops_gla_chunk_fwd": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
     "tops_gla_chunk_fwd_workspace_size": (C.c_size_t, [C.POINTER(ChunkFwdArgs)]),

@@ -635,3 +635,26 @@ def test_unfused_scan_and_output_path(gla):
     r = subprocess.run([sys.executable, "-c", _UNFUSED_CHILD, root], env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "UNFUSED_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_bounded_wait_timeout_is_reported_and_context_survives(gla):
+    """Failure path without a GPU fault: a kernel waits on an mbarrier that nothing will
+    complete; its bounded wait gives up (about 2 s), records code 1, and returns.  The host
+    reads the code, and the next operation runs normally."""
+    import ctypes
+
+    from tops import _C
+    _C.lib().tops_gla_device_error()  # clear anything earlier tests left
+    _C.call("tops_gla_selftest_wait_timeout", ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 1
+    rng = np.random.default_rng(5)
+    B, T, H, K, V = 1, 256, 2, 128, 128
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    bf = torch.bfloat16
+    o, ht = gla.chunk_gla(dev(q, bf), dev(k, bf), dev(v, bf), dev(g), output_final_state=True, chunk_size=64)
+    o_r, ht_r = O.chunk_gla(q, k, v, g, output_final_state=True, chunk_size=64)
+    assert_rel_l2("o after the timeout", o, o_r, BF16_L2)
+    assert _C.lib().tops_gla_device_error() == 0
