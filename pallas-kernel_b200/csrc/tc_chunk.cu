@@ -16,12 +16,19 @@
 //   k_prep : per (batch, chunk, head).  TMA loads q/k/g tiles, computes the gates in
 //            registers, writes qhat/kdec (TMA store) and D, and the intra-chunk matrix
 //            A with tcgen05.mma (accumulator in TMEM).
+//   k_scan_out : (default) per (batch, head, 128-wide V tile): the state scan fused with
+//            the chunk-output GEMM (fwd o, bwd dv); the state stays in TMEM and its bf16
+//            copy in shared memory feeds the output MMA, so the output never reads the
+//            chunk states back from HBM.
 //   k_scan : per (batch, head, 128-wide V tile).  Walks the chunks in order (or in
 //            reverse), state [K x 128] fp32 resident in TMEM, operands double
-//            buffered by TMA; optionally stores every chunk-start state in bf16.
-//   k_out  : persistent, warp specialised GEMM: TMA producer warp, MMA warp, four
-//            epilogue warps; 6-stage shared-memory ring, double-buffered TMEM
+//            buffered by TMA; optionally stores every chunk-start state in bf16.  Used
+//            for the zero-state span pass, the state-only entry points and the unfused path.
+//   k_out  : (unfused path) persistent, warp specialised GEMM: TMA producer warp, MMA warp,
+//            four epilogue warps; 6-stage shared-memory ring, double-buffered TMEM
 //            accumulator.  out[128 x 128] = X[128 x K] S[K x 128] + A'[128 x 128] Y[128 x 128].
+//   k_dqk  : per (batch, chunk, head, 64-wide K tile): dq, dk, dg from the chunk states
+//            h and dh, do, v, q, k and g (two CTAs per SM).
 // All waits are bounded (ptx::mbar_wait).  Shared-memory tiles use the 128-byte
 // swizzle that TMA writes and the UMMA descriptors describe.
 #include <cudaTypedefs.h>
