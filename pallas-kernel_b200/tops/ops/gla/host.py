@@ -25,16 +25,20 @@ class PinnedGLAPipeline:
     ``submit(q, k, v, g, do, out)`` enqueues one step (host tensors, pinned) and returns
     at once; ``synchronize()`` waits until every submitted step's gradients are in
     ``out``.  Slices of ``slice_batch`` sequences rotate through ``depth`` device slots.
+    The default slice is half the batch (rounded up): consecutive steps overlap each other,
+    so two slices per step keep both copy directions busy, and fewer, larger copies pay the
+    per-copy start cost less often (config 3 on one B200: 11.2 ms per step against 11.6 ms
+    with one-sequence slices; both copy directions at once take 10.5 ms).
     """
 
     def __init__(self, B, T, H, K, V, dtype=torch.bfloat16, scale=None, chunk_size: int = 64,
-                 slice_batch: int = 1, depth: int = 3, device=None):
+                 slice_batch: int | None = None, depth: int = 3, device=None):
         self.dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.B, self.T, self.H, self.K, self.V = B, T, H, K, V
         self.dtype = dtype
         self.scale = K ** -0.5 if scale is None else scale
         self.C = chunk_size
-        self.sb = max(1, min(slice_batch, B))
+        self.sb = max(1, min((B + 1) // 2 if slice_batch is None else slice_batch, B))
         self.depth = max(1, depth)
         sb, dev = self.sb, self.dev
         mk = lambda d, dt: torch.empty(sb, T, H, d, dtype=dt, device=dev)
