@@ -4,20 +4,23 @@
 //     h = h0 * e^{gk}[:,None] * e^{gv}[None,:] + k^T v,   o = (scale q)^T h,   ht = h.
 // The work is dominated by reading h0 and writing ht (fp32 [N,H,K,V]).  Each
 // (sequence, head) state is a contiguous K*V*4-byte tile, split into P row blocks
-// ("parts") of 32 KB.  A persistent CTA per SM streams its parts through a 6-stage
-// shared-memory ring: one thread issues 1D bulk copies (TMA) of the state part and
-// of the part's q/k/gk rows and v/gv vectors onto the stage's mbarrier; every thread
+// ("parts") of 32 KB.  A persistent CTA per SM (512 threads) streams its parts through
+// a 6-stage shared-memory ring: one thread issues 1D bulk copies (TMA) of the state part
+// and of the part's q/k/gk rows and v/gv vectors onto the stage's mbarrier; every thread
 // updates 16-byte column groups of the part's rows in registers, accumulates o, and
-// writes the new state straight to ht with coalesced 16-byte stores (a warp writes whole
-// 512-byte rows).  A stage is free as soon as it has been read, so five parts' loads
-// stay in flight while one is updated and HBM sees continuous read and write streams.
+// writes the new state straight to ht with coalesced 16-byte streaming stores (a warp
+// writes whole 512-byte rows; ht is not read again by the step, so its lines are marked
+// evict-first).  A stage is free as soon as it has been read, so five parts' loads stay
+// in flight while one is updated and HBM sees continuous read and write streams.  The
+// store stream needs the warps: 16 per SM reach 0.96 of the measured copy bandwidth at
+// config 2, 8 per SM (256 threads) 0.83.
 #include "common.cuh"
 #include "ptx.cuh"
 
 namespace tops {
 namespace decode {
 
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;
 constexpr int STAGES = 6;
 constexpr int AHEAD = STAGES - 1;  // loads in flight while one stage is updated
 constexpr int PART_BYTES = 32 * 1024;
@@ -116,7 +119,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode(Params p) {
       x.y = fmaf(kr, vc[1], x.y * d * ec[1]);
       x.z = fmaf(kr, vc[2], x.z * d * ec[2]);
       x.w = fmaf(kr, vc[3], x.w * d * ec[3]);
-      if (HAS_HT) *reinterpret_cast<float4*>(hrow + (size_t)r * V) = x;
+      if (HAS_HT) __stcs(reinterpret_cast<float4*>(hrow + (size_t)r * V), x);
       acc.x = fmaf(qr, x.x, acc.x);
       acc.y = fmaf(qr, x.y, acc.y);
       acc.z = fmaf(qr, x.z, acc.z);
