@@ -765,8 +765,10 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
 // shared memory in the 128-byte-swizzled layout of the B operand of the output GEMM, so
 // the output GEMM never reads the states back from HBM (the separate k_out does).  The
 // copy and the output tiles go to HBM through ordinary coalesced stores (whole rows per
-// warp instruction), not through the TMA unit, whose per-SM throughput (about 84 GB/s)
-// the operand loads (224 KB per chunk at K = 256) already need.
+// warp instruction), not through TMA stores: the CTA's TMA stream is bounded by the bytes
+// its ring keeps in flight (about 95 GB/s for 96 KB), which the operand loads (224 KB per
+// chunk at K = 256) already need (TMA stores measured 164 us per launch at config 3
+// against 152 us).
 //   warp 0      TMA producer: per chunk the y tile (v or do; 2 slots) and a ring of
 //               32 KB stages: the A tiles, output-side x tiles (qhat / kdec), scan-side x tiles
 //   warp 1      MMA issuer: o = A' Y (8 MMAs; needs no state, so it overlaps the state pass),
