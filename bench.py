@@ -181,7 +181,8 @@ def max_over_ranks(x: float, world: int) -> float:
 # CPU baseline: the oracle (numpy float32 restatement of the reference algorithm)
 # ---------------------------------------------------------------------------
 
-def cpu_sample(seconds_budget: float = 20.0, T: int = 1024):
+def cpu_sample(seconds_budget: float = 20.0, T: int = 4096):
+    """One whole config-3 sequence (all heads) through the oracle's fwd + bwd: ~10 s of CPU work."""
     import numpy as np
 
     from oracle import gla_oracle as O
