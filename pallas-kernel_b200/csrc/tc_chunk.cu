@@ -13,7 +13,7 @@
 // qhat_c^T do_c and dv_c = A_c^T do_c + kdec_c dh_c.
 //
 // Kernels
-//   k_prep : per (batch, chunk, head).  TMA loads q/k/g tiles, computes the gates in
+//   k_prep : persistent over (batch, chunk, head).  TMA loads q/k/g tiles, computes the gates in
 //            registers, writes qhat/kdec (TMA store) and D, and the intra-chunk matrix
 //            A with tcgen05.mma (accumulator in TMEM).
 //   k_scan_out : (default) per (batch, head, 128-wide V tile): the state scan fused with
@@ -124,7 +124,10 @@ __device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, uint32_t lane0
 }
 
 // ===========================================================================
-// k_prep: gates, qhat/kdec, D and the intra-chunk matrix A.  grid (NTb, H, B), 256 threads.
+// k_prep: gates, qhat/kdec, D and the intra-chunk matrix A.  Persistent: min(items, 2 x SMs)
+// CTAs of 256 threads (two per SM) walk the items (chunk, head, batch), chunk fastest; TMEM and
+// the barriers stay set up across items, and the next item's first gate tiles load while the
+// current item's last K block is gated.
 // ===========================================================================
 struct PrepParams {
   int B, T, H, K, NTb;
@@ -148,10 +151,17 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
   __shared__ __align__(8) uint64_t bar_g, bar_qk, bar_mma;
   __shared__ uint32_t tmem_base;
 
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row0 = c * BT;
   const int nkb = p.K / 64;
+  // persistent: this CTA takes items blockIdx.x, + gridDim.x, ...; item = (chunk, head, batch), chunk fastest
+  const int items = p.NTb * p.H * p.B;
+  auto coords = [&](int it_, int& c_, int& h_, int& b_) {
+    c_ = it_ % p.NTb;
+    h_ = (it_ / p.NTb) % p.H;
+    b_ = it_ / (p.NTb * p.H);
+  };
+  int c, h, b;
+  coords((int)blockIdx.x, c, h, b);
 
   if (warp == 0) {
     ptx::tmem_alloc(&tmem_base, 128);
@@ -162,11 +172,11 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
     ptx::mbar_init(&bar_qk, 1);
     ptx::mbar_init(&bar_mma, 1);
     ptx::fence_mbar_init();
-    // the gates of K block 0; each later block's gates load as soon as the previous
-    // block's gates are in registers (g tiles free), ahead of its q / k tiles
+    // the gates of K block 0; each later block's gates (and the next item's first) load as
+    // soon as the previous block's gates are in registers (g tiles free), ahead of its q / k
     ptx::mbar_arrive_expect_tx(&bar_g, 2 * TILE_BYTES);
-    ptx::tma_load_4d(gb, &maps.g, 0, h, row0, b, &bar_g);
-    ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, 32, h, row0, b, &bar_g);
+    ptx::tma_load_4d(gb, &maps.g, 0, h, c * BT, b, &bar_g);
+    ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, 32, h, c * BT, b, &bar_g);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -180,9 +190,13 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
   // halves in the opposite order so each 8-lane access phase touches 8 different bank groups
   const uint32_t go0 = (uint32_t)(c8 & 3) * 32 + ((c8 >> 2) ? 16u : 0u);
   bool ok = true;
-  for (int kbi = 0; kbi < nkb && ok; ++kbi) {
+  uint32_t kc = 0;  // K blocks processed by this CTA (mbarrier phases)
+  for (int it = (int)blockIdx.x; it < items && ok; it += (int)gridDim.x) {
+  coords(it, c, h, b);
+  const int row0 = c * BT;
+  for (int kbi = 0; kbi < nkb && ok; ++kbi, ++kc) {
     if (tid == 0) {
-      if (kbi > 0) ptx::bulk_wait_read<0>();  // previous qhat/kdec stores have read qb/kb
+      if (kc > 0) ptx::bulk_wait_read<0>();  // earlier stores (qhat/kdec, the last item's A) have read their tiles
       ptx::mbar_arrive_expect_tx(&bar_qk, 2 * TILE_BYTES);
       ptx::tma_load_4d(qb, &maps.q, kbi * 64, h, row0, b, &bar_qk);
       ptx::tma_load_4d(kb, &maps.k, kbi * 64, h, row0, b, &bar_qk);
@@ -191,7 +205,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
         ptx::tma_prefetch_4d(&maps.k, kbi * 64 + 64, h, row0, b);
       }
     }
-    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_g, (uint32_t)(kbi & 1)));  // uniform exit on a timeout
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_g, kc & 1u));  // uniform exit on a timeout
     if (!ok) break;
     const unsigned char* gt = gb + (c8 >> 2) * TILE_BYTES;
     float gv[4][8], ps[8];
@@ -219,11 +233,16 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       if (sub == 3) wtot[warp][c8 * 8 + j] = v;
     }
     __syncthreads();  // every thread holds its gates: the g tiles are free
-    if (tid == 0 && kbi + 1 < nkb) {
+    if (tid == 0 && (kbi + 1 < nkb || it + (int)gridDim.x < items)) {
+      int gc = c, gh = h, gbb = b, gk = kbi * 64 + 64;
+      if (kbi + 1 == nkb) {  // the next item's first K block
+        coords(it + (int)gridDim.x, gc, gh, gbb);
+        gk = 0;
+      }
       ptx::fence_async_smem();
       ptx::mbar_arrive_expect_tx(&bar_g, 2 * TILE_BYTES);
-      ptx::tma_load_4d(gb, &maps.g, kbi * 64 + 64, h, row0, b, &bar_g);
-      ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, kbi * 64 + 96, h, row0, b, &bar_g);
+      ptx::tma_load_4d(gb, &maps.g, gk, gh, gc * BT, gbb, &bar_g);
+      ptx::tma_load_4d(gb + TILE_BYTES, &maps.g, gk + 32, gh, gc * BT, gbb, &bar_g);
     }
     float off[8], gm[8], gl[8];
 #pragma unroll
@@ -255,7 +274,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       reinterpret_cast<float4*>(dp)[0] = make_float4(__expf(gl[0]), __expf(gl[1]), __expf(gl[2]), __expf(gl[3]));
       reinterpret_cast<float4*>(dp)[1] = make_float4(__expf(gl[4]), __expf(gl[5]), __expf(gl[6]), __expf(gl[7]));
     }
-    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_qk, (uint32_t)(kbi & 1)));
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_qk, kc & 1u));
     if (!ok) break;
     // all loads of the four rows first, then the arithmetic, then the stores (the
     // compiler cannot move loads across stores to buffers it cannot disambiguate)
@@ -309,7 +328,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       ptx::tma_store_4d(&maps.kd, kbi * 64, h, row0, b, kb);
       ptx::bulk_commit();
     }
-    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_mma, (uint32_t)(kbi & 1)));
+    ok = ptx::bar_and(1, 256, ptx::mbar_wait(&bar_mma, kc & 1u));
     ptx::tc_fence_after();
   }
   if (ok) {
@@ -343,6 +362,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       ptx::tma_store_4d(&maps.A, 64, h, row0, b, kt);
       ptx::bulk_commit();
     }
+  }
   }
   if (!ok && tid == 0) {  // drain loads that may still be in flight (bounded)
     ptx::mbar_wait(&bar_g, 0);
@@ -1823,7 +1843,8 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
     if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
       return cuda_status(e, "tc prep carveout");
-    k_prep<<<dim3(NTb, s.H, s.B), 256, prep_smem(), st>>>(pm, pp);
+    const int items = NTb * s.H * s.B;
+    k_prep<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
     TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   }
   int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, fused ? "tc_scan_out" : "tc_scan",
