@@ -421,6 +421,33 @@ def test_tc_backward_vs_oracle(gla, case):
     assert _C.lib().tops_gla_device_error() == 0
 
 
+def test_tc_with_the_api_default_chunk_size(gla):
+    """chunk_gla's default chunk_size (16, as in the reference) on bf16 inputs takes the tensor-core
+    path (which chunks by 128 internally: the result does not depend on the chunk size beyond
+    rounding); fwd + bwd vs the fp64 oracle at chunk size 16 (rel-L2 2e-2)."""
+    from tops import _C
+    from tops.ops.gla import _core
+    rng = np.random.default_rng(61)
+    B, T, H, K, V = 1, 300, 2, 128, 128
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 16).astype(np.float32)
+    do = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    bf = torch.bfloat16
+    qt, kt, vt = (dev(x, bf).requires_grad_() for x in (q, k, v))
+    gt = dev(g).requires_grad_()
+    assert _core.saved_size(_core.make_plan(qt, V, 16, None, K ** -0.5), gt) > 0, "should take the tensor-core path"
+    o, ht = gla.chunk_gla(qt, kt, vt, gt, output_final_state=True)
+    (o.float() * dev(do)).sum().backward()
+    o_r, ht_r = O.chunk_gla(q, k, v, g, output_final_state=True, chunk_size=16)
+    dq_r, dk_r, dv_r, dg_r, _ = O.chunk_gla_bwd(q, k, v, g, None, K ** -0.5, None, None, None, do, None, None, 16)
+    for nm, got, want in (("o", o, o_r), ("ht", ht, ht_r), ("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r),
+                          ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r)):
+        assert_rel_l2(nm, got, want, BF16_L2)
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
+
+
 def test_tc_long_sequence_takes_the_span_split_scan(gla):
     """A long single sequence (2 units, 128 chunks) runs its state scans as parallel spans."""
     from tops import _C
