@@ -16,6 +16,19 @@ from ._core import _cuda, _f32
 __all__ = ["fused_recurrent_gla", "fused_recurrent_gla_fwd", "fused_recurrent_gla_bwd"]
 
 
+def _bwd_operands(q, k, v, do):
+    """q, k, v, do for the backward kernel, which takes do in the storage type of q, k, v.
+
+    The forward output o is fp32, so its gradient arrives in fp32; the reference's backward
+    reads that gradient as it is (fused_recurrent.py:626-790).  Rather than round it to a
+    16-bit input type, the 16-bit q, k, v are widened to fp32 (exactly) and the kernel runs in
+    fp32 on the same values.
+    """
+    if do.dtype == torch.float32 and q.dtype != torch.float32:
+        return q.float(), k.float(), v.float(), do.contiguous()
+    return q, k, v, do.contiguous().to(q.dtype)
+
+
 def _validate(q, k, v, gk, gv, initial_state, cu_seqlens):
     B, T, H, K = q.shape
     V = v.shape[-1]
@@ -47,7 +60,8 @@ class _FusedRecurrentGLA(torch.autograd.Function):
     def backward(ctx, do, dht=None):
         q, k, v, gkc, gvc, h0c, o, cu_dev = ctx.saved_tensors
         scale, reverse, N, gk_dt, gv_dt = ctx.meta
-        dq, dk, dv, dgk, dgv, dh0 = _core.recurrent_bwd(q, k, v, gkc, gvc, h0c, o, do.contiguous().to(q.dtype),
+        qb, kb, vb, dob = _bwd_operands(q, k, v, do)
+        dq, dk, dv, dgk, dgv, dh0 = _core.recurrent_bwd(qb, kb, vb, gkc, gvc, h0c, o, dob,
                                                         None if dht is None else dht.float().contiguous(), scale,
                                                         reverse, cu_dev, N)
         dq, dk, dv = dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
@@ -100,6 +114,6 @@ def fused_recurrent_gla_bwd(q, k, v, gk=None, gv=None, o=None, do=None, dht=None
     assert gv is None or o is not None, "o (forward output) is required when gv is used"
     scale = scale if scale is not None else K ** -0.5
     q, k, v = (_cuda(n, x) for n, x in (("q", q), ("k", k), ("v", v)))
+    q, k, v, do = _bwd_operands(q, k, v, _cuda("do", do))
     return _core.recurrent_bwd(q, k, v, _f32("gk", gk), _f32("gv", gv), _f32("initial_state", initial_state),
-                               _f32("o", o), _cuda("do", do).to(q.dtype), _f32("dht", dht), float(scale),
-                               bool(reverse), cu_dev, N)
+                               _f32("o", o), do, _f32("dht", dht), float(scale), bool(reverse), cu_dev, N)

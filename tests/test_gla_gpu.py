@@ -315,6 +315,35 @@ def test_recurrent_autograd(gla):
         assert_close(nm, t.grad, r, atol=2e-4, rtol=2e-4)
 
 
+def test_recurrent_bf16_inputs_multi_step(gla):
+    """bf16 q, k, v over T > 1: o and ht come back in fp32 whatever the input dtype (as in the
+    reference, fused_recurrent.py:261-263) and match the oracle on the same bf16 values (fp32
+    1e-4); dq, dk, dv come back in bf16 (rel-L2 2e-2), dgk and dh0 in fp32."""
+    rng = np.random.default_rng(27)
+    B, T, H, K, V = 2, 37, 2, 64, 64
+    q, k = (GC.bf16_round(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = GC.bf16_round(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    gk = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 4).astype(np.float32)
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    dht = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    bf = torch.bfloat16
+    qt, kt, vt = (dev(x, bf).requires_grad_() for x in (q, k, v))
+    gkt, h0t = dev(gk).requires_grad_(), dev(h0).requires_grad_()
+    o, ht = gla.fused_recurrent_gla(qt, kt, vt, gk=gkt, initial_state=h0t, output_final_state=True)
+    assert o.dtype == torch.float32 and ht.dtype == torch.float32
+    o_r, ht_r = O.fused_recurrent_gla(q, k, v, gk, None, None, h0, True)
+    assert_close("o", o, o_r, **FP32)
+    assert_close("ht", ht, ht_r, **FP32)
+    ((o * dev(do)).sum() + (ht * dev(dht)).sum()).backward()
+    ref = O.fused_recurrent_gla_bwd(q, k, v, gk, None, do, dht, None, h0)
+    assert qt.grad.dtype == bf and gkt.grad.dtype == torch.float32
+    for nm, t, r in (("dq", qt, ref[0]), ("dk", kt, ref[1]), ("dv", vt, ref[2])):
+        assert_rel_l2(nm, t.grad, r, BF16_L2)
+    assert_close("dgk", gkt.grad, ref[3], atol=2e-4, rtol=2e-4)
+    assert_close("dh0", h0t.grad, ref[5], atol=2e-4, rtol=2e-4)
+
+
 def test_recurrent_k_split(gla):
     """K > 256 takes the K-split path with a workspace reduction."""
     rng = np.random.default_rng(5)
