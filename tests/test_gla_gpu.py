@@ -344,6 +344,40 @@ def test_recurrent_bf16_inputs_multi_step(gla):
     assert_close("dh0", h0t.grad, ref[5], atol=2e-4, rtol=2e-4)
 
 
+@pytest.mark.parametrize("op", ["chunk", "recurrent"])
+def test_fp16_inputs_fwd_bwd(gla, op):
+    """fp16 q, k, v (CUDA-core path for chunk_gla; the recurrence for fused_recurrent_gla):
+    chunk_gla returns o in fp16, fused_recurrent_gla in fp32, as in the reference; outputs and
+    gradients match the fp64 oracle on the same fp16 values within relative L2 2e-3."""
+    rng = np.random.default_rng(33 if op == "chunk" else 34)
+    B, T, H, K, V = 2, 70, 2, 32, 48
+    f16 = lambda x: x.astype(np.float16).astype(np.float32)
+    q, k = (f16(rng.standard_normal((B, T, H, K), dtype=np.float32)) for _ in range(2))
+    v = f16(rng.standard_normal((B, T, H, V), dtype=np.float32))
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 8).astype(np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    h16 = torch.float16
+    qt, kt, vt = (dev(x, h16).requires_grad_() for x in (q, k, v))
+    gt = dev(g).requires_grad_()
+    if op == "chunk":
+        do = f16(do)  # o is fp16, so its gradient is too
+        o, ht = gla.chunk_gla(qt, kt, vt, gt, output_final_state=True, chunk_size=16)
+        assert o.dtype == h16 and ht.dtype == torch.float32
+        o_r, ht_r = O.chunk_gla(q, k, v, g, output_final_state=True, chunk_size=16)
+        (o.float() * dev(do)).sum().backward()
+        dq_r, dk_r, dv_r, dg_r, _ = O.chunk_gla_bwd(q, k, v, g, None, K ** -0.5, None, None, None, do, None, None, 16)
+    else:
+        o, ht = gla.fused_recurrent_gla(qt, kt, vt, gk=gt, output_final_state=True)
+        assert o.dtype == torch.float32 and ht.dtype == torch.float32
+        o_r, ht_r = O.fused_recurrent_gla(q, k, v, g, None, None, None, True)
+        (o * dev(do)).sum().backward()
+        dq_r, dk_r, dv_r, dg_r = O.fused_recurrent_gla_bwd(q, k, v, g, None, do, None, None, None)[:4]
+    assert qt.grad.dtype == h16 and gt.grad.dtype == torch.float32
+    for nm, got, want in (("o", o, o_r), ("ht", ht, ht_r), ("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r),
+                          ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r)):
+        assert_rel_l2(nm, got, want, 2e-3)
+
+
 def test_recurrent_k_split(gla):
     """K > 256 takes the K-split path with a workspace reduction."""
     rng = np.random.default_rng(5)
