@@ -230,6 +230,29 @@ def test_fused_chunk_and_naive_agree(gla):
     assert_close("states", s1, s2, atol=1e-4, rtol=1e-4)
 
 
+def test_ungated_chunk_gla(gla):
+    """Neither g nor g_gamma (the reference's defaults: plain linear attention with state):
+    fwd + bwd match the oracle run with g=None (fp32 1e-4) and an explicit all-zero gate."""
+    rng = np.random.default_rng(13)
+    B, T, H, K, V = 2, 45, 2, 32, 24
+    q, k = (rng.standard_normal((B, T, H, K), dtype=np.float32) for _ in range(2))
+    v = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    qt, kt, vt, h0t = (dev(x).requires_grad_() for x in (q, k, v, h0))
+    o, ht = gla.chunk_gla(qt, kt, vt, initial_state=h0t, output_final_state=True)
+    (o * dev(do)).sum().backward()
+    o_r, ht_r = O.chunk_gla(q, k, v, None, initial_state=h0, output_final_state=True, chunk_size=16)
+    dq_r, dk_r, dv_r, _, dh0_r = O.chunk_gla_bwd(q, k, v, None, None, K ** -0.5, h0, None, None, do, None, None, 16)
+    for nm, got, want in (("o", o, o_r), ("ht", ht, ht_r), ("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r),
+                          ("dv", vt.grad, dv_r), ("dh0", h0t.grad, dh0_r)):
+        assert_close(nm, got, want, **FP32)
+    o0, ht0 = gla.chunk_gla(dev(q), dev(k), dev(v), torch.zeros(B, T, H, K, device="cuda"), initial_state=dev(h0),
+                            output_final_state=True)
+    assert_close("o vs g = 0", o.detach(), o0, **FP32)
+    assert_close("ht vs g = 0", ht.detach(), ht0, **FP32)
+
+
 def test_g_gamma_matches_broadcast_g(gla):
     rng = np.random.default_rng(12)
     B, T, H, K, V = 2, 48, 4, 32, 32
