@@ -191,6 +191,37 @@ def test_subfunctions_match_oracle(gla):
         assert_close(nm, a, b, **FP32)
 
 
+def test_common_chunk_h_entry_points(gla):
+    """tops.ops.common.chunk_h: chunk_fwd_h_ref / chunk_fwd_h_kernel / chunk_bwd_dh_kernel against
+    the oracle's state scans; with split_size = 2 chunks the kernel forms keep the state of the
+    first chunk of every split (as the reference stores it when i_t % (split / chunk) == 0)."""
+    from tops.ops.common import chunk_h as CH
+    rng = np.random.default_rng(71)
+    B, T, H, K, V, C = 2, 64, 2, 16, 24, 16
+    q, k = (rng.standard_normal((B, T, H, K), dtype=np.float32) for _ in range(2))
+    v = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    g = (GC.logsigmoid(rng.standard_normal((B, T, H, K))) / 4).astype(np.float32)
+    gc = O.chunk_local_cumsum(g, C).astype(np.float32)
+    h0 = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    do = rng.standard_normal((B, T, H, V), dtype=np.float32)
+    dht = rng.standard_normal((B, H, K, V), dtype=np.float32)
+    scale = K ** -0.5
+    h_r, ht_r = O.chunk_fwd_h(k, v, gc, h0, True, None, C)  # [B, NT, H, K, V]
+    h, ht = CH.chunk_fwd_h_ref(dev(k), dev(v), gk=dev(gc), h0=dev(h0), output_final_state=True,
+                               states_in_fp32=True, chunk_size=C)
+    assert_close("h (ref form)", h, h_r, **FP32)
+    assert_close("ht (ref form)", ht, ht_r, **FP32)
+    hs, ht2 = CH.chunk_fwd_h_kernel(dev(k), dev(v), gk=dev(gc), h0=dev(h0), output_final_state=True, chunk_size=C,
+                                    split_size=2 * C, states_in_fp32=True)
+    assert_close("h (kernel form, split 2)", hs, h_r.reshape(-1, H, K, V)[::2], **FP32)
+    assert_close("ht (kernel form)", ht2, ht_r, **FP32)
+    dh_r, dh0_r = O.chunk_bwd_dh(q, k, v, gc, do, None, dht, scale, None, C)
+    dhs, dh0 = CH.chunk_bwd_dh_kernel(dev(q), dev(k), dev(v), gk=dev(gc), do=dev(do), dht=dev(dht), scale=scale,
+                                      output_dh0=True, chunk_size=C, split_size=2 * C, states_in_fp32=True)
+    assert_close("dh (kernel form, split 2)", dhs, dh_r.reshape(-1, H, K, V)[::2], **FP32)
+    assert_close("dh0 (kernel form)", dh0, dh0_r, **FP32)
+
+
 # ---------------------------------------------------------------------------
 # structural behaviour (reference test_pallas_chunk_gla.py:223-273)
 # ---------------------------------------------------------------------------
