@@ -168,9 +168,15 @@ TOPS_API int tops_gla_chunk_bwd(const tops_gla_chunk_bwd_args* a, void* stream);
  * fixed array of TOPS_GLA_NOALLOC_SCRATCH_BYTES inside the library's device image,
  * one per GPU that loads the library, held until the process exits.  Problems whose
  * scratch (tops_gla_chunk_fwd_workspace_size) exceeds it are rejected with
- * TOPS_ERR_WORKSPACE.  The first call on a device looks up that device's array
- * address (make it before any stream capture).  All calls on a device share the
- * array: calls whose kernels overlap on the GPU race. */
+ * TOPS_ERR_WORKSPACE.  CUDA loads the library's device image on a GPU lazily, so the
+ * first call on a device (unless another of this library's kernels ran there before)
+ * loads it and thereby reserves the 16 MiB: a host that must not allocate after
+ * start-up makes one warm-up call per device at start-up, before any stream capture.
+ * Every call looks up the array's address on the current device (a host-side symbol
+ * lookup), so a cudaDeviceReset or another context does not leave a stale address.
+ * All calls on a device share the one array and it keeps the last call's contents:
+ * calls whose kernels may overlap on the GPU (different streams, no ordering between
+ * them) race and give wrong results; order them on one stream or with events. */
 #define TOPS_GLA_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 TOPS_API int tops_gla_chunk_fwd_noalloc(const tops_gla_chunk_fwd_args* a, void* stream);
 TOPS_API size_t tops_gla_chunk_bwd_workspace_size(const tops_gla_chunk_bwd_args* a);

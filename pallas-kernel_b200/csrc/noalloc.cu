@@ -9,15 +9,18 @@
 // in a fixed-size array that is part of this library's device image.
 //
 // Properties of the array:
-//  * TOPS_GLA_NOALLOC_SCRATCH_BYTES (16 MiB), reserved on every GPU that loads
-//    the library and held until the process exits;
+//  * TOPS_GLA_NOALLOC_SCRATCH_BYTES (16 MiB) per GPU, placed when the library's
+//    device image is loaded on that GPU and held until the process exits.  CUDA
+//    loads device images lazily (the default since CUDA 12.2), so that happens at
+//    the first use of any of the library's kernels there -- possibly this entry
+//    point's first call, which then reserves the 16 MiB itself.  A host that must
+//    not allocate after start-up makes one warm-up call per device at start-up,
+//    before any stream capture;
 //  * one array per device, shared by every call on that device: two calls whose
 //    kernels overlap on the GPU (different streams, no ordering) race on it;
 //  * it keeps the previous call's contents; the forward writes every scratch
 //    element it reads (the only buffer that must start at zero, the gate sums when
 //    g is NULL, is cleared in-stream by the forward itself).
-#include <mutex>
-
 #include "common.cuh"
 
 namespace tops {
@@ -25,27 +28,22 @@ namespace noalloc {
 
 static __device__ __align__(256) unsigned char g_scratch[TOPS_GLA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-static std::mutex g_mu;
-static void* g_addr[kMaxDevices] = {};
-
-// Device address of this device's scratch array (set-up on the first call per device,
-// with that device current).  In host code `g_scratch` is only a host-side stand-in
-// for the symbol, never a usable address.
+// Device address of the current device's scratch array, looked up on every call with
+// that device current.  The first call on a device loads this library's device image
+// there (CUDA loads modules lazily), which places the array; later calls are a host-side
+// symbol lookup.  Not cached: a cudaDeviceReset or a different context current on the
+// same device places the array at another address, and a cached address would then point
+// at freed or foreign memory.  In host code `g_scratch` is only a host-side stand-in for
+// the symbol, never a usable address.
 static int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "chunk_fwd_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) return fail(TOPS_ERR_UNSUPPORTED, "chunk_fwd_noalloc: device ordinal too large");
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (g_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "chunk_fwd_noalloc: cudaGetSymbolAddress");
-    if (p == nullptr) return fail(TOPS_ERR_CUDA, "chunk_fwd_noalloc: scratch symbol has no device address");
-    g_addr[dev] = p;
-  }
-  *out = g_addr[dev];
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "chunk_fwd_noalloc: cudaGetSymbolAddress");
+  if (p == nullptr) return fail(TOPS_ERR_CUDA, "chunk_fwd_noalloc: scratch symbol has no device address");
+  *out = p;
   return TOPS_OK;
 }
 

@@ -39,3 +39,14 @@ def assert_rel_l2(name, got, want, tol):
     assert np.isfinite(g).all(), f"{name}: non-finite values"
     r = rel_l2(g, w)
     assert r <= tol, f"{name}: relative L2 error {r:.3e} > {tol}"
+
+
+def assert_max_rel(name, got, want, tol):
+    """Element-wise bound relative to the tensor's scale: max |got - want| <= tol * max |want|.
+    Catches one bad tile or row that a relative-L2 check over a large tensor would average away."""
+    g, w = to_np(got), to_np(want)
+    assert g.shape == w.shape, f"{name}: shape {g.shape} != {w.shape}"
+    assert np.isfinite(g).all(), f"{name}: non-finite values"
+    err = float(np.abs(g - w).max()) if g.size else 0.0
+    scale = float(np.abs(w).max()) if w.size else 0.0
+    assert err <= tol * max(scale, 1e-30), f"{name}: max abs error {err:.3e} > {tol} x max |ref| {scale:.3e}"

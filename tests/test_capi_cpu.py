@@ -112,3 +112,41 @@ def test_jax_frontend_imports_where_jax_exists():
     pytest.importorskip("jax")
     import tops.jax as TJ  # noqa: F401
     assert callable(TJ.chunk_gla)
+
+
+def test_noalloc_lookup_path_without_a_device(lib):
+    """The allocation-free forward looks up its array's address per call; without a usable
+    device that lookup fails with a CUDA status and a message, it neither crashes nor uses a
+    host-side stand-in address.  Oversized problems are rejected before any lookup."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("checks the no-device path")
+    L = lib.lib()
+    s = lib.Shape(2, 32, 4, 32, 64, 2, 4, 16, lib.F32, 0.1, None, None)
+    a = lib.ChunkFwdArgs(s, 1, 1, 1, None, None, 1, None, None, None, None, None, 0)
+    rc = L.tops_gla_chunk_fwd_noalloc(ctypes.byref(a), None)
+    assert rc == -3, rc  # TOPS_ERR_CUDA
+    assert b"chunk_fwd_noalloc" in L.tops_gla_last_error()
+    big = lib.Shape(8, 4096, 4, 256, 512, 8, 8 * 64, 64, lib.F32, 0.0625, None, None)
+    b = lib.ChunkFwdArgs(big, 1, 1, 1, None, None, 1, None, None, None, None, None, 0)
+    assert L.tops_gla_chunk_fwd_noalloc(ctypes.byref(b), None) == -4  # TOPS_ERR_WORKSPACE
+    assert b"more than the fixed" in L.tops_gla_last_error()
+
+
+def test_xla_custom_call_failure_reaches_the_status(lib, tmp_path):
+    """A malformed descriptor given to an XLA custom-call target is reported through
+    XlaCustomCallStatusSetFailure (resolved from the host process at run time; here a C
+    stand-in loaded globally) before anything touches the device."""
+    src, so = tmp_path / "status.c", tmp_path / "libxla_status_standin.so"
+    src.write_text("#include <stddef.h>\n#include <string.h>\n"
+                   "void XlaCustomCallStatusSetFailure(void* st, const char* m, size_t n) {"
+                   " char* s = (char*)st; size_t k = n < 254 ? n : 254; s[0] = 1; memcpy(s + 1, m, k); s[1 + k] = 0; }\n")
+    subprocess.run(["gcc", "-shared", "-fPIC", str(src), "-o", str(so)], check=True)
+    ctypes.CDLL(str(so), mode=ctypes.RTLD_GLOBAL)
+    L = lib.lib()
+    for name in ("tops_gla_xla_chunk_fwd", "tops_gla_xla_chunk_bwd", "tops_gla_xla_recurrent_fwd"):
+        st = ctypes.create_string_buffer(256)
+        arr = (ctypes.c_void_p * 1)(None)
+        getattr(L, name)(None, ctypes.cast(arr, ctypes.c_void_p), b"\x00" * 7, 7, ctypes.cast(st, ctypes.c_void_p))
+        assert st.raw[0] == 1, name
+        assert b"bad descriptor" in st.raw, st.raw[:80]
