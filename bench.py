@@ -409,6 +409,17 @@ def run_ours(args):
     # ---- long context (config 4) ---------------------------------------------------
     lc = long_context_bench(args, world, rank, local, dev)
 
+    # ---- configs 3 and 2 at their stated global sizes split over the ranks (strong) ----
+    strong = {}
+    if world > 1:
+        strong["cfg3"] = strong_cfg3_bench(args, world, rank, dev)
+        if CFG2["B"] % world == 0:
+            d2 = decode_bench(args, world, local, dev, B=CFG2["B"] // world)
+            strong["cfg2"] = {**d2, "scaling": "strong",
+                              "metric": "fused_recurrent_gla decode step, global B=256 split over the ranks"}
+    else:
+        strong["note"] = "at one GPU the strong-scaling legs are the headline (config 3) and decode (config 2)"
+
     # ---- config-5 model training step (GLA layers + SwiGLU, data parallel) -----------
     torch.cuda.empty_cache()
     lm = None if args.no_model else model_bench(args, world, rank, local, dev)
@@ -428,7 +439,8 @@ def run_ours(args):
                            "K": K, "V": V, "chunk_size": C, "global_batch": B * world,
                            "parallelism": f"batch x heads shards, {world} GPU(s), no collective",
                            "l2": "inputs (537 MB/step) larger than L2; no flush"},
-                "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc, "model_dp": lm,
+                "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc,
+                "strong_scaling": strong, "model_dp": lm,
                 "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
@@ -438,12 +450,12 @@ def run_ours(args):
     return 0
 
 
-def decode_bench(args, world, local, dev):
+def decode_bench(args, world, local, dev, B=None):
     import torch
 
     from tops.ops.gla import _core
     c = CFG2
-    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    B, T, H, K, V = c["B"] if B is None else B, c["T"], c["H"], c["K"], c["V"]
     gen = torch.Generator(device=dev).manual_seed(7)
     bf = torch.bfloat16
     q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
@@ -507,9 +519,11 @@ def decode_bench(args, world, local, dev):
 
 def long_context_bench(args, world, rank, local, dev):
     """Config 4: chunk_gla fwd+bwd over one long sequence.  1 GPU: the whole sequence (state
-    scans split into parallel spans).  N GPUs: rank r holds tokens [r T/N, (r+1) T/N); the
-    forward runs a state-only pass, all-gathers (final state, span decay) and re-runs from its
-    incoming state; the backward does the same with dh0 (tops.distributed, NCCL)."""
+    scans split into parallel spans).  N GPUs: rank r holds tokens [r T/N, (r+1) T/N) and runs
+    tops.distributed.chunk_gla_seq_parallel with the C ABI's NCCL state exchange: the forward's
+    first phase (gating, zero-state span scans) yields the span's (final state, decay), one
+    all-gather + prefix gives its incoming state, the second phase finishes the scan and the
+    output; the backward does the same with the span's dh0."""
     import torch
 
     from tops.ops.gla import _core
@@ -530,16 +544,13 @@ def long_context_bench(args, world, rank, local, dev):
             return _core.chunk_bwd(plan, q, k, v, g, None, do, None, block=sv.get("block"))
     else:
         from tops import distributed as TD
+        ex = TD.NcclStateExchange()
+        for x in (q, k, v, g):
+            x.requires_grad_()
 
         def step():
-            S = _core.final_state(plan, q, k, v, g, None)
-            D = _core.span_decay(plan, g)
-            S_all, D_all = TD.all_gather_stack(S), TD.all_gather_stack(D)
-            H_in = TD.prefix_states(S_all, D_all, None)[rank]
-            o, _, sv = _core.chunk_fwd(plan, q, k, v, g, H_in, False, save=True)
-            L = _core.initial_state_grad(plan, q, k, v, g, H_in, do, None, block=sv.get("block"))
-            G = TD.suffix_grads(TD.all_gather_stack(L), D_all, None)[rank]
-            return _core.chunk_bwd(plan, q, k, v, g, H_in, do, G, want_dh0=True, block=sv.get("block"))
+            o, _ = TD.chunk_gla_seq_parallel(q, k, v, g, chunk_size=C, exchange=ex)
+            return torch.autograd.grad(o, (q, k, v, g), do)
 
     for _ in range(3):
         step()
@@ -553,12 +564,58 @@ def long_context_bench(args, world, rank, local, dev):
     e1.record(s)
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    if world > 1:
+        torch.cuda.synchronize()
+        ex.close()
     del q, k, v, g, do
     return {"metric": "chunk_gla fwd+bwd tokens/s, long context (BASELINE config 4)", "value": B * T / (ms * 1e-3),
             "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
             "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "T_per_gpu": Tr,
                        "parallelism": "1 GPU (state scans in parallel spans)" if world == 1 else
-                       f"sequence spans over {world} GPUs, all-gather of span states and dh0 (NCCL)"}}
+                       f"sequence spans over {world} GPUs, two-phase span fwd/bwd, one NCCL all-gather "
+                       "of (state, decay) per direction"}}
+
+
+def strong_cfg3_bench(args, world, rank, dev):
+    """Config 3 at its stated global size, B = 8 sequences split over the ranks (strong
+    scaling: B/N sequences per GPU, no collective).  At N = 8 a GPU holds one sequence (16
+    (head, V-tile) scan units), so the state scans run in parallel spans."""
+    import torch
+
+    from tops.ops.gla import _core
+    c = CFG3
+    Bg, T, H, K, V, C = 8, c["T"], c["H"], c["K"], c["V"], c["C"]
+    if Bg % world:
+        return None
+    B = Bg // world
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
+    do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    plan = _core.make_plan(q, V, C, None, K ** -0.5)
+
+    def step():
+        o, _, sv = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+        return _core.chunk_bwd(plan, q, k, v, g, None, do, None, block=sv.get("block"))
+
+    for _ in range(3):
+        step()
+    steps = max(5, args.steps)
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    return {"metric": "chunk_gla fwd+bwd tokens/s, config 3 at its global size (strong scaling)",
+            "value": Bg * T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "scaling": "strong", "config": {"global_batch": Bg, "B_per_gpu": B, "T": T, "H": H, "K": K, "V": V,
+                                            "chunk_size": C, "inputs_bytes_per_gpu": B * T * H * (6 * K + 4 * V)}}
 
 
 def model_bench(args, world, rank, local, dev):

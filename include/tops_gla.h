@@ -272,6 +272,36 @@ TOPS_API int tops_gla_span_decay(const tops_gla_shape* s, const float* g, float*
 TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, const float* decay, const float* h_in,
                            const float* s_local, float* out, void* stream);
 
+/* ---- sequence-parallel forward / backward in two phases ---
+ * No reference counterpart (the reference has no multi-device code); the math is the
+ * linear decomposition of its chunked scan (tops/ops/common/chunk_h.py:372-386).  Each rank
+ * holds one contiguous span of a long sequence (fixed length, tensor-core path: bf16,
+ * K in {128, 256}, V % 128 == 0).  The scan is linear in the span's incoming state, so the
+ * first phase does all the work that does not depend on it and returns the span's own
+ * final state from a zero state (local_state [N,H,K,V] fp32) and its total decay
+ * (decay [N,H,K] fp32, exp of the span's gate sums); the host exchanges these between ranks
+ * (tops_gla_state_exchange, or any all-gather + prefix) and the second phase finishes from
+ * the span's incoming state.  Per rank the two phases cost what one tops_gla_chunk_fwd
+ * (tops_gla_chunk_bwd) costs, plus one small combine kernel.
+ *  - the saved block (a->saved, tops_gla_chunk_span_saved_size bytes) is written by
+ *    fwd_span_begin and read by fwd_span_finish and both backward phases;
+ *  - fwd_span_finish: a->h0 = the span's incoming state (NULL = zero), a->o out, a->ht
+ *    (optional) = the span's final state;
+ *  - bwd_span_begin: local_dh0 = gradient w.r.t. the span's incoming state of the span's
+ *    own loss (a zero final-state gradient); a->workspace (tops_gla_chunk_bwd_span_
+ *    workspace_size bytes) holds state between the two backward calls: pass the same one;
+ *  - bwd_span_finish: a->dht = the gradient w.r.t. the span's final state from the later
+ *    spans (NULL = zero), outputs dq, dk, dv, dg and (optional) dh0.
+ * Other problems get TOPS_ERR_UNSUPPORTED; use tops_gla_chunk_fwd with o == NULL and
+ * tops_gla_chunk_bwd with NULL gradients for them. */
+TOPS_API size_t tops_gla_chunk_span_saved_size(const tops_gla_shape* s);
+TOPS_API int tops_gla_chunk_fwd_span_begin(const tops_gla_chunk_fwd_args* a, float* local_state, float* decay,
+                                           void* stream);
+TOPS_API int tops_gla_chunk_fwd_span_finish(const tops_gla_chunk_fwd_args* a, void* stream);
+TOPS_API size_t tops_gla_chunk_bwd_span_workspace_size(const tops_gla_chunk_bwd_args* a);
+TOPS_API int tops_gla_chunk_bwd_span_begin(const tops_gla_chunk_bwd_args* a, float* local_dh0, void* stream);
+TOPS_API int tops_gla_chunk_bwd_span_finish(const tops_gla_chunk_bwd_args* a, void* stream);
+
 /* ---- sequence-parallel state exchange over NCCL ---------
  * Every rank holds one contiguous span of a long sequence.  Forward (backward = 0):
  * local_state = the span's final state from a zero state S [N,H,K,V] (tops_gla_chunk_fwd

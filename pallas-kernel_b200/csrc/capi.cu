@@ -124,6 +124,17 @@ int fwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, co
         void* o, float* ht, void* saved, void* workspace, cudaStream_t st);
 int read_device_error();
 int selftest_wait_timeout(cudaStream_t st);
+size_t span_saved_bytes(const tops_gla_shape& s);
+size_t bwd_span_workspace(const tops_gla_shape& s);
+int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, void* saved,
+                   float* local_state, float* decay, cudaStream_t st);
+int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const float* h_in, void* o, float* ht, void* saved, cudaStream_t st);
+int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, void* workspace, float* local_dh0,
+                   cudaStream_t st);
+int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const void* dO, const float* dht_in, const void* saved, void* dq, void* dk, void* dv, float* dg,
+                    float* dh0, void* workspace, cudaStream_t st);
 size_t bwd_workspace(const tops_gla_shape& s, bool have_saved);
 int bwd(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, const float* h0,
         const void* dO, const float* dht, const void* saved, void* dq, void* dk, void* dv, float* dg, float* dh0,
@@ -284,6 +295,20 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
   return simt::bwd_dqkg(s, a->q, a->k, a->v, hh, gcc, a->do_, dh, dqi, dki, a->dq, a->dk, s.dtype, a->dg, st);
 }
 
+// the two-phase span entry points serve fixed-length problems on the tensor-core path
+static int check_span(const tops_gla_shape* s, const void* saved, size_t saved_bytes, const float* g) {
+  int rc = check_shape(s);
+  if (rc) return rc;
+  TOPS_CHECK_ARG(s->cu_seqlens == nullptr, "span entry points: variable-length input is not supported");
+  TOPS_CHECK_ARG(g != nullptr, "span entry points: g is required");
+  if (!tc::eligible(*s))
+    return fail(TOPS_ERR_UNSUPPORTED, "span entry points: the problem does not run on the tensor-core path");
+  TOPS_CHECK_ARG(saved != nullptr, "span entry points: the saved block is required");
+  if (saved_bytes < tc::span_saved_bytes(*s))
+    return fail(TOPS_ERR_WORKSPACE, "span entry points: saved block smaller than tops_gla_chunk_span_saved_size()");
+  return TOPS_OK;
+}
+
 static int check_rec(const tops_gla_recurrent_args* a) {
   TOPS_CHECK_ARG(a != nullptr, "args is NULL");
   TOPS_CHECK_ARG(a->B >= 0 && a->T >= 0 && a->H >= 0 && a->K > 0 && a->V > 0, "bad dimension");
@@ -390,6 +415,57 @@ size_t tops_gla_chunk_bwd_workspace_size(const tops_gla_chunk_bwd_args* a) {
   size_t need = 0;
   if (chunk_bwd_impl(a, nullptr, &need) != TOPS_OK) return 0;
   return need;
+}
+
+size_t tops_gla_chunk_span_saved_size(const tops_gla_shape* s) {
+  if (check_shape(s) != TOPS_OK || s->cu_seqlens != nullptr || !tc::eligible(*s)) return 0;
+  return tc::span_saved_bytes(*s);
+}
+
+int tops_gla_chunk_fwd_span_begin(const tops_gla_chunk_fwd_args* a, float* local_state, float* decay, void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_fwd_span_begin: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc) return rc;
+  TOPS_CHECK_ARG(a->q && a->k && a->v && local_state && decay,
+                 "chunk_fwd_span_begin: q, k, v, local_state and decay are required");
+  return tc::fwd_span_begin(a->s, a->q, a->k, a->v, a->g, a->saved, local_state, decay, S(stream));
+}
+
+int tops_gla_chunk_fwd_span_finish(const tops_gla_chunk_fwd_args* a, void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_fwd_span_finish: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc) return rc;
+  TOPS_CHECK_ARG(a->q && a->k && a->v && a->o, "chunk_fwd_span_finish: q, k, v and o are required");
+  return tc::fwd_span_finish(a->s, a->q, a->k, a->v, a->g, a->h0, a->o, a->ht, a->saved, S(stream));
+}
+
+size_t tops_gla_chunk_bwd_span_workspace_size(const tops_gla_chunk_bwd_args* a) {
+  if (a == nullptr || check_shape(&a->s) != TOPS_OK || a->s.cu_seqlens != nullptr || !tc::eligible(a->s)) return 0;
+  return tc::bwd_span_workspace(a->s);
+}
+
+static int check_bwd_span_ws(const tops_gla_chunk_bwd_args* a) {
+  if (a->workspace == nullptr || a->workspace_bytes < tc::bwd_span_workspace(a->s))
+    return fail(TOPS_ERR_WORKSPACE, "span entry points: workspace smaller than tops_gla_chunk_bwd_span_workspace_size()");
+  return TOPS_OK;
+}
+
+int tops_gla_chunk_bwd_span_begin(const tops_gla_chunk_bwd_args* a, float* local_dh0, void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_bwd_span_begin: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc || (rc = check_bwd_span_ws(a))) return rc;
+  TOPS_CHECK_ARG(a->do_ && local_dh0, "chunk_bwd_span_begin: do and local_dh0 are required");
+  return tc::bwd_span_begin(a->s, a->do_, a->saved, a->workspace, local_dh0, S(stream));
+}
+
+int tops_gla_chunk_bwd_span_finish(const tops_gla_chunk_bwd_args* a, void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_bwd_span_finish: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc || (rc = check_bwd_span_ws(a))) return rc;
+  TOPS_CHECK_ARG(a->q && a->k && a->v && a->do_ && a->dq && a->dk && a->dv && a->dg,
+                 "chunk_bwd_span_finish: q, k, v, do and dq, dk, dv, dg are required");
+  return tc::bwd_span_finish(a->s, a->q, a->k, a->v, a->g, a->do_, a->dht, a->saved, a->dq, a->dk, a->dv, a->dg,
+                             a->dh0, a->workspace, S(stream));
 }
 
 int tops_gla_recurrent_fwd(const tops_gla_recurrent_args* a, void* stream) {

@@ -606,6 +606,28 @@ __global__ void k_span_prefix(int S, int B, int H, int K, int V, const float* __
   }
 }
 
+// A rank's whole span from the per-span results of a zero-state pass (E, P): its final state
+// from a zero state, out = fold over spans (out <- P_s out + E_s, from 0), and optionally its
+// total decay dout = prod_s P_s (per state row).  One thread per 4 consecutive state columns.
+__global__ void k_span_total(int S, int B, int H, int K, int V, const float* __restrict__ P,
+                             const float* __restrict__ E, float* __restrict__ out, float* __restrict__ dout) {
+  const size_t n4 = (size_t)B * H * K * V / 4;
+  const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n4) return;
+  const size_t per = (size_t)B * H * K * V, rows = (size_t)B * H * K;
+  const size_t row = idx * 4 / V;  // (b*H + h)*K + k
+  float4 cur = make_float4(0.f, 0.f, 0.f, 0.f);
+  float dp = 1.f;
+  for (int s = 0; s < S; ++s) {
+    const float d = P[s * rows + row];
+    const float4 x = reinterpret_cast<const float4*>(E + s * per)[idx];
+    cur = make_float4(fmaf(d, cur.x, x.x), fmaf(d, cur.y, x.y), fmaf(d, cur.z, x.z), fmaf(d, cur.w, x.w));
+    dp *= d;
+  }
+  reinterpret_cast<float4*>(out)[idx] = cur;
+  if (dout != nullptr && (idx * 4) % V == 0) dout[row] = dp;
+}
+
 // ===========================================================================
 // k_out: persistent GEMM  out[128 x 128] = X[128 x K] S[K x 128] + A'[128 x 128] Y[128 x 128]
 // per item (batch, chunk, head, V tile).  grid = #SMs, 192 threads.
@@ -1569,8 +1591,10 @@ static int sm_count() {
 }
 
 // Span split of the state scans: enough spans that the scan grid fills the SMs (one CTA
-// per SM: 512 TMEM columns), at least 16 chunks per span; one span when the (batch, head,
-// V-tile) units alone fill half the GPU or the sequence is short.
+// per SM: 512 TMEM columns), at least 8 chunks per span; one span when the (batch, head,
+// V-tile) units alone fill half the GPU or the sequence is short.  A split runs every chunk
+// twice (the zero-state pass, which has no output GEMM, then the re-scan), in exchange for a
+// chain of NTb / spans chunks per CTA instead of NTb.
 struct Spans {
   int n, len;
 };
@@ -1578,9 +1602,9 @@ static Spans spans_for(const tops_gla_shape& s, int NTb) {
   const int units = (s.V / BV) * s.H * s.B;
   const int nsm = sm_count();
   Spans r{1, NTb};
-  if (units * 2 > nsm || NTb < 32) return r;
+  if (units * 2 > nsm || NTb < 16) return r;
   int S = nsm / units;
-  if (S > NTb / 16) S = NTb / 16;
+  if (S > NTb / 8) S = NTb / 8;
   if (S < 2) return r;
   r.len = (NTb + S - 1) / S;
   r.n = (NTb + r.len - 1) / r.len;
@@ -1592,8 +1616,9 @@ static Spans spans_for(const tops_gla_shape& s, int NTb) {
 struct SpanBufs {
   float *E = nullptr, *Hs = nullptr, *P = nullptr;
 };
-static size_t carve_spans(const tops_gla_shape& s, Spans spn, char* base, size_t off, SpanBufs* out) {
-  if (spn.n <= 1) return off;
+static size_t carve_spans(const tops_gla_shape& s, Spans spn, char* base, size_t off, SpanBufs* out,
+                          bool force = false) {
+  if (spn.n <= 1 && !force) return off;
   auto take = [&](size_t bytes) {
     off = (off + 1023) & ~size_t(1023);
     char* p = base ? base + off : nullptr;
@@ -1702,7 +1727,9 @@ struct Saved {
   SpanBufs sb;  // scratch of a span-split forward scan (empty when the scan runs in one span)
 };
 
-static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv, bool spans = true) {
+// force_spans: carve the span scratch even for one span (the two-phase sequence-parallel entry
+// points keep the zero-state pass's results there between their two calls)
+static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv, bool spans = true, bool force_spans = false) {
   const int NTb = (s.T + BT - 1) / BT;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1718,7 +1745,7 @@ static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv, bool s
   v.A = reinterpret_cast<bf16*>(take(tok * BT * 2));
   v.D = reinterpret_cast<float*>(take((size_t)s.B * NTb * s.H * s.K * 4));
   v.h = reinterpret_cast<bf16*>(take((size_t)s.B * NTb * s.H * s.K * s.V * 2));
-  if (spans) off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb);
+  if (spans) off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb, force_spans);
   if (sv) *sv = v;
   return off;
 }
@@ -1734,6 +1761,48 @@ static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 2 * TILE_BY
 template <typename KernelT>
 static cudaError_t set_smem(KernelT k, size_t bytes) {
   return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// First launch of a span-split scan: every span from a zero state, its final state into
+// sb.E and the product of its chunk decays into sb.P (also for a single span).
+static int scan_spans_zero(const tops_gla_shape& s, const ScanMaps& sm, int reverse, const float* D,
+                           const SpanBufs& sb, Spans spn, cudaStream_t st) {
+  const int NTb = (s.T + BT - 1) / BT;
+  cudaError_t e;
+  if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
+  ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P, nullptr};
+  k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+  TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
+  return TOPS_OK;
+}
+
+// Rest of a span-split scan after scan_spans_zero: every span's incoming state from `init`
+// (k_span_prefix; a single span starts from `init` itself), then the re-scan from those
+// states that stores the chunk states (and, with `fm`, writes the chunk outputs).
+static int scan_spans_finish(const tops_gla_shape& s, const ScanMaps& sm, int reverse, const float* D,
+                             const float* init, float* fin, bf16* states, const SpanBufs& sb, Spans spn,
+                             cudaStream_t st, const char* name, const FusedMaps* fm) {
+  const int NTb = (s.T + BT - 1) / BT;
+  cudaError_t e;
+  if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
+  if (fm && (e = set_smem(k_scan_out<false>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
+  const float* span_init = init;
+  if (spn.n > 1) {
+    LaunchTimer lt(st, "tc_span_prefix");
+    const size_t n4 = (size_t)s.B * s.H * s.K * s.V / 4;
+    k_span_prefix<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, init, sb.P, sb.E, sb.Hs);
+    TOPS_CUDA_LAUNCH_CHECK("tc_span_prefix");
+    span_init = sb.Hs;
+  }
+  LaunchTimer lt(st, name);
+  ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, span_init, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
+  if (fm)
+    k_scan_out<false><<<dim3(s.V / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+  else
+    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+  TOPS_CUDA_LAUNCH_CHECK(name);
+  return TOPS_OK;
 }
 
 // One state scan (forward h or reverse dh), split into spans when that fills the GPU.
@@ -1769,28 +1838,8 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
-  {
-    LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P, nullptr};
-    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
-    TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
-  }
-  {
-    LaunchTimer lt(st, "tc_span_prefix");
-    const size_t n4 = (size_t)s.B * s.H * s.K * s.V / 4;
-    k_span_prefix<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, init, sb.P, sb.E, sb.Hs);
-    TOPS_CUDA_LAUNCH_CHECK("tc_span_prefix");
-  }
-  {
-    LaunchTimer lt(st, name);
-    ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, sb.Hs, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
-    if (fm)
-      k_scan_out<false><<<dim3(s.V / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
-    else
-      k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
-    TOPS_CUDA_LAUNCH_CHECK(name);
-  }
-  return TOPS_OK;
+  int rc = scan_spans_zero(s, sm, reverse, D, sb, spn, st);
+  return rc ? rc : scan_spans_finish(s, sm, reverse, D, init, fin, states, sb, spn, st, name, fm);
 }
 
 // The fused scan + output kernel is the default; TOPS_GLA_UNFUSED_OUT=1 selects the
@@ -1803,6 +1852,36 @@ static bool fused_out() {
   return on;
 }
 
+// Tensor maps of k_prep (q, k, g in; qhat, kdec, A out) and of the forward state scan
+// (kdec, v in; chunk states out) over the saved block `sv`.
+static bool fwd_maps(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                     const Saved& sv, PrepMaps* pm, ScanMaps* sm) {
+  const int NTb = (s.T + BT - 1) / BT;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return map_tok(&pm->q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&pm->k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&pm->g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
+         map_tok(&pm->qh, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&pm->kd, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&pm->A, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT) &&
+         map_tok(&sm->x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&sm->y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+         map_state_store(&sm->st, sv.h, s.B * NTb * s.H, s.K, s.V);
+}
+
+static int launch_prep(const tops_gla_shape& s, const PrepMaps& pm, const Saved& sv, cudaStream_t st) {
+  const int NTb = (s.T + BT - 1) / BT;
+  cudaError_t e;
+  LaunchTimer lt(st, "tc_prep");
+  PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
+  if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
+  if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+    return cuda_status(e, "tc prep carveout");
+  const int items = NTb * s.H * s.B;
+  k_prep<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
+  TOPS_CUDA_LAUNCH_CHECK("tc_prep");
+  return TOPS_OK;
+}
+
 // Forward of a fixed-length (or padded varlen, blk_off != null) problem: o, ht and (in
 // `saved`) qhat, kdec, A, D, chunk-start states h.
 static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
@@ -1811,16 +1890,10 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   Saved sv;
   carve_saved(s, saved, &sv, blk_off == nullptr);
   const int NTb = (s.T + BT - 1) / BT;
-  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   PrepMaps pm;
-  bool okm = map_tok(&pm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&pm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-             map_tok(&pm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
-             map_tok(&pm.qh, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-             map_tok(&pm.kd, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-             map_tok(&pm.A, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
   ScanMaps sm;
-  okm = okm && map_tok(&sm.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_tok(&sm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_state_store(&sm.st, sv.h, s.B * NTb * s.H, s.K, s.V);
+  bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm);
   OutMaps om;
   FusedMaps fm;
   const bool fused = o != nullptr && fused_out();
@@ -1837,17 +1910,9 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   fm.out = static_cast<bf16*>(o);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
-  {
-    LaunchTimer lt(st, "tc_prep");
-    PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
-    if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
-    if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
-      return cuda_status(e, "tc prep carveout");
-    const int items = NTb * s.H * s.B;
-    k_prep<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
-    TOPS_CUDA_LAUNCH_CHECK("tc_prep");
-  }
-  int rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, fused ? "tc_scan_out" : "tc_scan",
+  int rc = launch_prep(s, pm, sv, st);
+  if (rc) return rc;
+  rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, fused ? "tc_scan_out" : "tc_scan",
                     blk_off, fused ? &fm : nullptr);
   if (rc) return rc;
   if (o == nullptr || fused) return TOPS_OK;  // final state only, or o written by the fused scan
@@ -1864,6 +1929,51 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
 }
 
 static size_t dqk_smem() { return 2 * (size_t)DQK_STG + 1024; }
+
+// reverse scan: qhat (saved) and do in, chunk-end state gradients dh out
+static bool bwd_scan_maps(const tops_gla_shape& s, const void* dO, const Saved& sv, bf16* dhs, ScanMaps* sm) {
+  const int NTb = (s.T + BT - 1) / BT;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return map_tok(&sm->x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&sm->y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+         map_state_store(&sm->st, dhs, s.B * NTb * s.H, s.K, s.V);
+}
+
+// fused reverse scan + dv GEMM: qhat / kdec / A (saved) and do in, dv out
+static bool bwd_fused_maps(const tops_gla_shape& s, const void* dO, void* dv, const Saved& sv, FusedMaps* fm) {
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  fm->out = static_cast<bf16*>(dv);
+  return map_tok(&fm->sx, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&fm->y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+         map_tok(&fm->ox, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&fm->a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64);
+}
+
+static bool dqk_maps(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                     const void* dO, const Saved& sv, bf16* dhs, void* dq, void* dk, float* dg, DqkMaps* dm) {
+  const int NTb = (s.T + BT - 1) / BT;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  return map_tok(&dm->dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_tok(&dm->v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+         map_state(&dm->hs, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
+         map_state(&dm->dhs, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
+         map_tok(&dm->g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm->dg, dg, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
+         map_tok(&dm->q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&dm->dq, dq, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
+}
+
+static int launch_dqk(const tops_gla_shape& s, const DqkMaps& dm, void* dq, void* dk, float* dg, cudaStream_t st) {
+  const int NTb = (s.T + BT - 1) / BT;
+  cudaError_t e;
+  LaunchTimer lt(st, "tc_dqk");
+  DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
+  if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
+  // two CTAs per SM need the largest shared-memory carveout
+  if ((e = cudaFuncSetAttribute(k_dqk, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+    return cuda_status(e, "tc dqk carveout");
+  k_dqk<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
+  TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
+  return TOPS_OK;
+}
 
 // workspace of bwd_core: dh states, span scratch, and the saved block when it is recomputed
 static size_t bwd_core_workspace(const tops_gla_shape& s, bool have_saved, bool spans) {
@@ -1894,11 +2004,9 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   }
   Saved sv;
   carve_saved(s, saved, &sv, blk_off == nullptr);
-  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   ScanMaps sm;
-  bool okm = map_tok(&sm.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-             map_tok(&sm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
-             map_state_store(&sm.st, dhs, s.B * NTb * s.H, s.K, s.V);
+  bool okm = bwd_scan_maps(s, dO, sv, dhs, &sm);
   const bool dh0_only = dq == nullptr;  // dq, dk, dv, dg all NULL: the reverse scan alone
   if (dh0_only) {
     if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
@@ -1907,25 +2015,15 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   OutMaps om;
   FusedMaps fm;
   const bool fused = fused_out();
-  fm.out = static_cast<bf16*>(dv);
   if (fused)
-    okm = okm && map_tok(&fm.sx, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-          map_tok(&fm.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
-          map_tok(&fm.ox, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-          map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64);
+    okm = okm && bwd_fused_maps(s, dO, dv, sv, &fm);
   else
     okm = okm && map_tok(&om.x, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_state(&om.s, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
           map_tok(&om.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, 64) &&
           map_tok(&om.y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, 64) && map_tok(&om.o, dv, BF, 2, s.B, s.T, s.H, s.V, 64, BT);
   DqkMaps dm;
-  okm = okm && map_tok(&dm.dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
-        map_tok(&dm.v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
-        map_state(&dm.hs, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
-        map_state(&dm.dhs, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
-        map_tok(&dm.g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.dg, dg, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm.q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_tok(&dm.k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm.dq, dq, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-        map_tok(&dm.dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
+  okm = okm && dqk_maps(s, q, k, v, g, dO, sv, dhs, dq, dk, dg, &dm);
   if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
   if ((rc = run_scan(s, sm, 1, sv.D, dht, dh0, dhs, sb, spn, st, fused ? "tc_scan_out_bwd" : "tc_scan_bwd", blk_off,
@@ -1940,17 +2038,107 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     k_out<<<grid, 192, out_smem(), st>>>(om, op);
     TOPS_CUDA_LAUNCH_CHECK("tc_out_dv");
   }
-  {
-    LaunchTimer lt(st, "tc_dqk");
-    DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
-    if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
-    // two CTAs per SM need the largest shared-memory carveout
-    if ((e = cudaFuncSetAttribute(k_dqk, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
-      return cuda_status(e, "tc dqk carveout");
-    k_dqk<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
-    TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
-  }
+  return launch_dqk(s, dm, dq, dk, dg, st);
+}
+
+// ---------------------------------------------------------------------------
+// Two-phase forward / backward of one span of a sequence split over ranks (fixed length).
+// The scan is linear in its incoming state, so everything that does not depend on it runs
+// in the first phase: k_prep and the zero-state pass of the span-split scan, whose per-span
+// results (E, P) stay in the saved block (forward) or the workspace (backward) and are also
+// folded into the span's own final state S and decay D.  The host exchanges (S, D) between
+// ranks; the second phase forms every in-GPU span's incoming state from the rank's incoming
+// state (k_span_prefix) and runs the fused re-scan and, backward, k_dqk.  Per rank this is
+// the single-GPU work plus one small combine kernel per direction.
+// ---------------------------------------------------------------------------
+static Spans spans_of(const tops_gla_shape& s) { return spans_for(s, (s.T + BT - 1) / BT); }
+
+size_t span_saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nullptr, true, true); }
+
+static int span_total(const tops_gla_shape& s, Spans spn, const SpanBufs& sb, float* out, float* dout,
+                      cudaStream_t st) {
+  LaunchTimer lt(st, "tc_span_total");
+  const size_t n4 = (size_t)s.B * s.H * s.K * s.V / 4;
+  k_span_total<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, sb.P, sb.E, out, dout);
+  TOPS_CUDA_LAUNCH_CHECK("tc_span_total");
   return TOPS_OK;
+}
+
+int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, void* saved,
+                   float* local_state, float* decay, cudaStream_t st) {
+  Saved sv;
+  carve_saved(s, saved, &sv, true, true);
+  PrepMaps pm;
+  ScanMaps sm;
+  if (!fwd_maps(s, q, k, v, g, sv, &pm, &sm)) return fail(TOPS_ERR_CUDA, "tc fwd span: cuTensorMapEncodeTiled failed");
+  const Spans spn = spans_of(s);
+  int rc;
+  if ((rc = launch_prep(s, pm, sv, st)) || (rc = scan_spans_zero(s, sm, 0, sv.D, sv.sb, spn, st))) return rc;
+  return span_total(s, spn, sv.sb, local_state, decay, st);
+}
+
+int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const float* h_in, void* o, float* ht, void* saved, cudaStream_t st) {
+  Saved sv;
+  carve_saved(s, saved, &sv, true, true);
+  PrepMaps pm;
+  ScanMaps sm;
+  FusedMaps fm;
+  const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm) && map_tok(&fm.sx, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+                   map_tok(&fm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+                   map_tok(&fm.ox, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+                   map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
+  fm.out = static_cast<bf16*>(o);
+  if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd span: cuTensorMapEncodeTiled failed");
+  return scan_spans_finish(s, sm, 0, sv.D, h_in, ht, sv.h, sv.sb, spans_of(s), st, "tc_scan_out", &fm);
+}
+
+// backward workspace of the two-phase entry points: dh states and the span scratch
+size_t bwd_span_workspace(const tops_gla_shape& s) {
+  const int NTb = (s.T + BT - 1) / BT;
+  const size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
+  return (carve_spans(s, spans_of(s), nullptr, n, nullptr, true) + 1023) & ~size_t(1023);
+}
+
+static void carve_bwd_span(const tops_gla_shape& s, void* workspace, bf16** dhs, SpanBufs* sb) {
+  const int NTb = (s.T + BT - 1) / BT;
+  char* ws = static_cast<char*>(workspace);
+  *dhs = reinterpret_cast<bf16*>(ws);
+  const size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
+  carve_spans(s, spans_of(s), ws, n, sb, true);
+}
+
+int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, void* workspace, float* local_dh0,
+                   cudaStream_t st) {
+  Saved sv;
+  carve_saved(s, const_cast<void*>(saved), &sv, true, true);
+  bf16* dhs;
+  SpanBufs sb;
+  carve_bwd_span(s, workspace, &dhs, &sb);
+  ScanMaps sm;
+  if (!bwd_scan_maps(s, dO, sv, dhs, &sm)) return fail(TOPS_ERR_CUDA, "tc bwd span: cuTensorMapEncodeTiled failed");
+  const Spans spn = spans_of(s);
+  int rc = scan_spans_zero(s, sm, 1, sv.D, sb, spn, st);
+  return rc ? rc : span_total(s, spn, sb, local_dh0, nullptr, st);
+}
+
+int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
+                    const void* dO, const float* dht_in, const void* saved, void* dq, void* dk, void* dv, float* dg,
+                    float* dh0, void* workspace, cudaStream_t st) {
+  Saved sv;
+  carve_saved(s, const_cast<void*>(saved), &sv, true, true);
+  bf16* dhs;
+  SpanBufs sb;
+  carve_bwd_span(s, workspace, &dhs, &sb);
+  ScanMaps sm;
+  FusedMaps fm;
+  DqkMaps dm;
+  const bool okm = bwd_scan_maps(s, dO, sv, dhs, &sm) && bwd_fused_maps(s, dO, dv, sv, &fm) &&
+                   dqk_maps(s, q, k, v, g, dO, sv, dhs, dq, dk, dg, &dm);
+  if (!okm) return fail(TOPS_ERR_CUDA, "tc bwd span: cuTensorMapEncodeTiled failed");
+  int rc = scan_spans_finish(s, sm, 1, sv.D, dht_in, dh0, dhs, sb, spans_of(s), st, "tc_scan_out_bwd", &fm);
+  return rc ? rc : launch_dqk(s, dm, dq, dk, dg, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -106,6 +106,12 @@ SIGNATURES = {
     "tops_gla_chunk_bwd_dqk_intra": (C.c_int, [C.POINTER(Shape), VP, VP, VP, VP, VP, VP, VP]),
     "tops_gla_chunk_bwd_dqkg": (C.c_int, [C.POINTER(Shape), VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, VP, I32, VP,
                                           VP]),
+    "tops_gla_chunk_span_saved_size": (C.c_size_t, [C.POINTER(Shape)]),
+    "tops_gla_chunk_fwd_span_begin": (C.c_int, [C.POINTER(ChunkFwdArgs), VP, VP, VP]),
+    "tops_gla_chunk_fwd_span_finish": (C.c_int, [C.POINTER(ChunkFwdArgs), VP]),
+    "tops_gla_chunk_bwd_span_workspace_size": (C.c_size_t, [C.POINTER(ChunkBwdArgs)]),
+    "tops_gla_chunk_bwd_span_begin": (C.c_int, [C.POINTER(ChunkBwdArgs), VP, VP]),
+    "tops_gla_chunk_bwd_span_finish": (C.c_int, [C.POINTER(ChunkBwdArgs), VP]),
     "tops_gla_span_decay": (C.c_int, [C.POINTER(Shape), VP, VP, VP]),
     "tops_gla_state_combine": (C.c_int, [I32, I32, I32, I32, VP, VP, VP, VP, VP]),
     "tops_gla_norm_gate_fwd": (C.c_int, [C.c_int64, I32, I32, F32C, VP, VP, VP, VP, VP, VP]),

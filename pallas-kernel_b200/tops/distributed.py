@@ -31,7 +31,8 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["shard", "prefix_states", "suffix_grads", "all_gather_stack", "seq_parallel_forward",
-           "seq_parallel_backward", "chunk_gla_seq_parallel", "NcclStateExchange"]
+           "seq_parallel_backward", "seq_parallel_forward_phased", "seq_parallel_backward_phased",
+           "chunk_gla_seq_parallel", "NcclStateExchange"]
 
 
 class NcclStateExchange:
@@ -130,6 +131,47 @@ def suffix_grads(dh0_local: torch.Tensor, D: torch.Tensor, dht: torch.Tensor | N
     return torch.stack(out, 0)
 
 
+def _exchange_forward(S, D, h0, group, exchange):
+    """(this rank's incoming state, the whole sequence's final state) from every rank's (S, D)."""
+    if exchange is not None:
+        return exchange.forward(S, D, h0)
+    rank = dist.get_rank(group)
+    S_all = all_gather_stack(S, group)
+    D_all = all_gather_stack(D.to(S.dtype), group)
+    H_all = prefix_states(S_all, D_all, h0)
+    return H_all[rank], D_all[-1][..., None] * H_all[-1] + S_all[-1]
+
+
+def _exchange_backward(L, D, dht, group, exchange):
+    """The final-state gradient this rank's backward must use, from every rank's (L, D)."""
+    if exchange is not None:
+        return exchange.backward(L, D, dht)
+    L_all = all_gather_stack(L, group)
+    D_all = all_gather_stack(D.to(L.dtype), group)
+    return suffix_grads(L_all, D_all, dht)[dist.get_rank(group)]
+
+
+def seq_parallel_forward_phased(begin: Callable, finish: Callable, h0=None, group=None,
+                                exchange: NcclStateExchange | None = None):
+    """Forward of one rank's span in two phases (no recomputation).
+
+    begin() -> (S, D): everything that does not depend on the incoming state, returning the
+    span's final state from a zero state and its decay; finish(H_in) -> o completes the span
+    from its incoming state.  Returns (o, H_in, ht_global, D).
+    """
+    S, D = begin()
+    H_in, ht_global = _exchange_forward(S, D, h0, group, exchange)
+    return finish(H_in), H_in, ht_global, D
+
+
+def seq_parallel_backward_phased(begin: Callable, finish: Callable, D: torch.Tensor, dht=None, group=None,
+                                 exchange: NcclStateExchange | None = None):
+    """Backward of one rank's span in two phases: begin() -> the gradient of the span's own loss
+    w.r.t. its incoming state; finish(G) -> the gradients, G being the final-state gradient from
+    the later spans (``dht`` for the last)."""
+    return finish(_exchange_backward(begin(), D, dht, group, exchange))
+
+
 def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, h0=None, group=None,
                          local_final: Callable | None = None, exchange: NcclStateExchange | None = None):
     """Forward of one rank's span.
@@ -142,19 +184,10 @@ def seq_parallel_forward(local_fwd: Callable, span_decay: Callable, q, k, v, g, 
     H_in is this rank's incoming state and ht_global the final state of the whole sequence
     (identical on all ranks).
     """
-    rank = dist.get_rank(group)
     S = local_final(q, k, v, g) if local_final is not None else local_fwd(q, k, v, g, None)[1]
     D = span_decay(g)
-    if exchange is not None:
-        H_in, ht_global = exchange.forward(S, D, h0)
-        o, _ = local_fwd(q, k, v, g, H_in)
-        return o, H_in, ht_global
-    S_all = all_gather_stack(S, group)
-    D_all = all_gather_stack(D.to(S.dtype), group)
-    H_all = prefix_states(S_all, D_all, h0)
-    H_in = H_all[rank]
-    o, ht_local = local_fwd(q, k, v, g, H_in)
-    ht_global = D_all[-1][..., None] * H_all[-1] + S_all[-1]
+    H_in, ht_global = _exchange_forward(S, D, h0, group, exchange)
+    o, _ = local_fwd(q, k, v, g, H_in)
     return o, H_in, ht_global
 
 
@@ -168,14 +201,8 @@ def seq_parallel_backward(local_bwd: Callable, D: torch.Tensor, H_in, do, dht=No
     whole sequence's final state (read by the last rank).  Returns (dq, dk, dv, dg, dh0) where
     dh0 is the gradient w.r.t. this rank's incoming state (rank 0: the user's initial state).
     """
-    rank = dist.get_rank(group)
     dh0_local = local_dh0(H_in, do) if local_dh0 is not None else local_bwd(H_in, do, None)[-1]
-    if exchange is not None:
-        return local_bwd(H_in, do, exchange.backward(dh0_local, D, dht))
-    L_all = all_gather_stack(dh0_local, group)
-    D_all = all_gather_stack(D.to(dh0_local.dtype), group)
-    G_all = suffix_grads(L_all, D_all, dht)
-    return local_bwd(H_in, do, G_all[rank])
+    return local_bwd(H_in, do, _exchange_backward(dh0_local, D, dht, group, exchange))
 
 
 class _SeqParallelChunkGLA(torch.autograd.Function):
@@ -184,6 +211,22 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
         from .ops.gla import _core
 
         p = _core.make_plan(q, v.shape[-1], chunk_size, None, scale)
+        ctx.plan, ctx.group, ctx.has_h0, ctx.exchange = p, group, h0 is not None, exchange
+        if _core.span_saved_size(p, g) > 0:
+            # tensor-core path: two phases, nothing computed twice
+            blk = {}
+
+            def begin():
+                S, D, blk["b"] = _core.fwd_span_begin(p, q, k, v, g)
+                return S, D
+
+            def finish(h_in):
+                return _core.fwd_span_finish(p, q, k, v, g, h_in, blk["b"])[0]
+
+            o, H_in, ht, D = seq_parallel_forward_phased(begin, finish, h0, group, exchange)
+            ctx.save_for_backward(q, k, v, g, H_in, D)
+            ctx.phased, ctx.fwd_saved = True, blk["b"]
+            return o, ht
         saved = {}
 
         def local_fwd(q_, k_, v_, g_, h_):
@@ -196,17 +239,32 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
 
         o, H_in, ht = seq_parallel_forward(local_fwd, lambda g_: _core.span_decay(p, g_), q, k, v, g, h0, group,
                                            local_final=local_final, exchange=exchange)
-        ctx.save_for_backward(q, k, v, g, H_in)
-        ctx.fwd_saved = saved
-        ctx.plan, ctx.group, ctx.has_h0, ctx.exchange = p, group, h0 is not None, exchange
+        ctx.save_for_backward(q, k, v, g, H_in, None)
+        ctx.phased, ctx.fwd_saved = False, saved
         return o, ht
 
     @staticmethod
     def backward(ctx, do, dht):
         from .ops.gla import _core
 
-        q, k, v, g, H_in = ctx.saved_tensors
+        q, k, v, g, H_in, D = ctx.saved_tensors
         p, sv = ctx.plan, ctx.fwd_saved
+        rank = dist.get_rank(ctx.group)
+        want = ctx.has_h0 and rank == 0
+        do = do.contiguous().to(q.dtype)
+        dht = None if dht is None else dht.float()
+        if ctx.phased:
+            ws = {}
+
+            def begin():
+                L, ws["w"] = _core.bwd_span_begin(p, q, k, v, g, do, sv)
+                return L
+
+            def finish(G):
+                return _core.bwd_span_finish(p, q, k, v, g, do, G, sv, ws["w"], want_dh0=want)
+
+            dq, dk, dv, dg, dh0 = seq_parallel_backward_phased(begin, finish, D, dht, ctx.group, ctx.exchange)
+            return dq, dk, dv, dg, dh0, None, None, None, None
 
         def local_bwd(h_in, do_, dht_):
             return _core.chunk_bwd(p, q, k, v, g, h_in, do_, dht_, sv.get("g_cumsum"), sv.get("A"), sv.get("h"),
@@ -216,12 +274,9 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
             return _core.initial_state_grad(p, q, k, v, g, h_in, do_, None, block=sv.get("block"))
 
         D = _core.span_decay(p, g)
-        dq, dk, dv, dg, dh0 = seq_parallel_backward(local_bwd, D, H_in, do.contiguous().to(q.dtype),
-                                                    None if dht is None else dht.float(), ctx.group,
+        dq, dk, dv, dg, dh0 = seq_parallel_backward(local_bwd, D, H_in, do, dht, ctx.group,
                                                     local_dh0=local_dh0, exchange=ctx.exchange)
-        rank = dist.get_rank(ctx.group)
-        d_h0 = dh0 if (ctx.has_h0 and rank == 0) else None
-        return dq, dk, dv, dg, d_h0, None, None, None, None
+        return dq, dk, dv, dg, dh0 if want else None, None, None, None, None
 
 
 def chunk_gla_seq_parallel(q, k, v, g, scale=None, initial_state=None, chunk_size=64, group=None, exchange=None):
@@ -232,7 +287,9 @@ def chunk_gla_seq_parallel(q, k, v, g, scale=None, initial_state=None, chunk_siz
     Returns (o of this span, final state of the whole sequence).  The only communication
     is two all-gathers of [B, H, K, V] fp32 states (+ [B, H, K] decays) per direction
     (torch.distributed, or the C ABI's NCCL exchange when ``exchange`` is an
-    ``NcclStateExchange``).
+    ``NcclStateExchange``).  On the tensor-core path the span runs in two phases (the C
+    ABI's tops_gla_chunk_{fwd,bwd}_span_{begin,finish}): the work that does not depend on
+    the incoming state runs before the exchange and is not repeated after it.
     """
     if scale is None:
         scale = q.shape[-1] ** -0.5

@@ -172,6 +172,72 @@ def initial_state_grad(p: Plan, q, k, v, g, h0, do, dht, block=None):
 
 
 # ---------------------------------------------------------------------------
+# two-phase span forward / backward (one rank's span of a sequence-parallel problem)
+# ---------------------------------------------------------------------------
+
+def span_saved_size(p: Plan, g) -> int:
+    """Bytes of the saved block of the two-phase span entry points (0: not served, i.e. the
+    problem does not run on the tensor-core path or is variable-length)."""
+    if g is None or p.cu_dev is not None:
+        return 0
+    return int(_C.lib().tops_gla_chunk_span_saved_size(p.shape()))
+
+
+def fwd_span_begin(p: Plan, q, k, v, g):
+    """Phase 1 of a span's forward -> (local_state [N,H,K,V] from a zero state, decay [N,H,K],
+    saved block)."""
+    dev = q.device
+    blk = torch.empty(span_saved_size(p, g), dtype=torch.uint8, device=dev)
+    S = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev)
+    D = torch.empty(p.N, p.H, p.K, dtype=torch.float32, device=dev)
+    a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), None, None, None,
+                        None, None, None, None, 0, _C.ptr(blk), blk.numel())
+    _C.call("tops_gla_chunk_fwd_span_begin", a, _C.ptr(S), _C.ptr(D), _C.stream_of(q))
+    return S, D, blk
+
+
+def fwd_span_finish(p: Plan, q, k, v, g, h_in, blk, want_ht: bool = False):
+    """Phase 2: the span's output from its incoming state ``h_in`` -> (o, ht|None)."""
+    dev = q.device
+    o = torch.empty(p.B, p.T, p.H, p.V, dtype=q.dtype, device=dev)
+    ht = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_ht else None
+    a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), _C.ptr(h_in), _C.ptr(o), _C.ptr(ht),
+                        None, None, None, None, 0, _C.ptr(blk), blk.numel())
+    _C.call("tops_gla_chunk_fwd_span_finish", a, _C.stream_of(q))
+    return o, ht
+
+
+def _span_bwd_args(p: Plan, q, k, v, g, do, dht, blk, outs=(None,) * 5):
+    dq, dk, dv, dg, dh0 = outs
+    return _C.ChunkBwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), None, _C.ptr(do), _C.ptr(dht),
+                           None, None, None, _C.ptr(dq), _C.ptr(dk), _C.ptr(dv), _C.ptr(dg), _C.ptr(dh0), None, 0,
+                           _C.ptr(blk), blk.numel())
+
+
+def bwd_span_begin(p: Plan, q, k, v, g, do, blk):
+    """Phase 1 of a span's backward -> (local dh0 of the span's own loss, workspace to pass on)."""
+    a = _span_bwd_args(p, q, k, v, g, do, None, blk)
+    ws = torch.empty(max(int(_C.lib().tops_gla_chunk_bwd_span_workspace_size(a)), 1), dtype=torch.uint8,
+                     device=q.device)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), ws.numel()
+    L = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=q.device)
+    _C.call("tops_gla_chunk_bwd_span_begin", a, _C.ptr(L), _C.stream_of(q))
+    return L, ws
+
+
+def bwd_span_finish(p: Plan, q, k, v, g, do, dht_in, blk, ws, want_dh0: bool = False):
+    """Phase 2: gradients from the final-state gradient ``dht_in`` -> (dq, dk, dv, dg, dh0|None)."""
+    dev = q.device
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(p.B, p.T, p.H, p.K, dtype=torch.float32, device=dev)
+    dh0 = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=dev) if want_dh0 else None
+    a = _span_bwd_args(p, q, k, v, g, do, dht_in, blk, (dq, dk, dv, dg, dh0))
+    a.workspace, a.workspace_bytes = _C.ptr(ws), ws.numel()
+    _C.call("tops_gla_chunk_bwd_span_finish", a, _C.stream_of(q))
+    return dq, dk, dv, dg, dh0
+
+
+# ---------------------------------------------------------------------------
 # sub-functions
 # ---------------------------------------------------------------------------
 

@@ -71,13 +71,20 @@ def _worker(rank, world, port, out):
 
     K = q.shape[-1]
     dq, dk, dv, dg, dh0 = TD.seq_parallel_backward(local_bwd, decay(gs), H_in, dos, t(dht))
+    # the two-phase form (begin before the exchange, finish after it) must give the same
+    o2, H2, ht2, D2 = TD.seq_parallel_forward_phased(lambda: (local_fwd(qs, ks, vs, gs, None)[1], decay(gs)),
+                                                     lambda h_in: local_fwd(qs, ks, vs, gs, h_in)[0], t(h0))
+    grads2 = TD.seq_parallel_backward_phased(lambda: local_bwd(H2, dos, None)[-1],
+                                             lambda G: local_bwd(H2, dos, G), D2, t(dht))
+    phased = dict(o=o2.numpy(), ht=ht2.numpy(), **{nm: x.numpy() for nm, x in zip(("dq", "dk", "dv", "dg", "dh0"),
+                                                                                  grads2)})
     # batch sharding: each rank's slice of the batch equals the full run's slice
     ob = None
     if q.shape[0] % world == 0:
         qb, kb, vb, gb = (TD.shard(t(x), rank, world) for x in (q, k, v, g))
         ob, _ = local_fwd(qb, kb, vb, gb, None)
     out[rank] = dict(o=o.numpy(), ht=ht.numpy(), dq=dq.numpy(), dk=dk.numpy(), dv=dv.numpy(), dg=dg.numpy(),
-                     dh0=dh0.numpy(), ob=None if ob is None else ob.numpy())
+                     dh0=dh0.numpy(), ob=None if ob is None else ob.numpy(), phased=phased)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -106,6 +113,13 @@ def test_seq_parallel_and_batch_shard_gloo(world):
     for nm, ref in (("dq", dq_r), ("dk", dk_r), ("dv", dv_r), ("dg", dg_r)):
         np.testing.assert_allclose(np.concatenate([out[r][nm] for r in range(world)], 1), ref, **tol)
     np.testing.assert_allclose(out[0]["dh0"], dh0_r, **tol)
+    ph = [out[r]["phased"] for r in range(world)]
+    np.testing.assert_allclose(np.concatenate([x["o"] for x in ph], 1), o_ref, **tol)
+    for nm, ref in (("dq", dq_r), ("dk", dk_r), ("dv", dv_r), ("dg", dg_r)):
+        np.testing.assert_allclose(np.concatenate([x[nm] for x in ph], 1), ref, err_msg=f"phased {nm}", **tol)
+    for r in range(world):
+        np.testing.assert_allclose(ph[r]["ht"], ht_ref, **tol)
+    np.testing.assert_allclose(ph[0]["dh0"], dh0_r, **tol)
     if q.shape[0] % world == 0:
         o_nostate, _ = O.chunk_gla(q, k, v, g, chunk_size=16)
         np.testing.assert_allclose(np.concatenate([out[r]["ob"] for r in range(world)], 0), o_nostate, **tol)
