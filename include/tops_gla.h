@@ -334,6 +334,18 @@ TOPS_API int tops_gla_state_exchange(const tops_gla_exchange_args* a, void* stre
 TOPS_API int tops_gla_nccl_get_unique_id(void* id);
 TOPS_API int tops_gla_nccl_comm_init(void** comm, int32_t world, const void* id, int32_t rank);
 TOPS_API int tops_gla_nccl_comm_destroy(void* comm);
+/* Failure handling.  A lost peer is best detected on the host before an exchange is
+ * launched (the Python host checks a heartbeat of every rank first); these cover what
+ * happens after a launch.  comm_abort: ncclCommAbort (ends the communicator's in-flight
+ * work without waiting for peers; the handle is freed, do not destroy it afterwards).
+ * comm_check: TOPS_OK, or TOPS_ERR_NCCL with NCCL's asynchronous error.  exchange_wait:
+ * waits on the host, at most timeout_ms, for the work enqueued on `stream` so far (the
+ * exchange) while polling the communicator's asynchronous error; on an error or at the
+ * deadline it aborts the communicator and returns TOPS_ERR_NCCL / TOPS_ERR_TIMEOUT instead of
+ * blocking.  No reference counterpart (the reference has no multi-device code). */
+TOPS_API int tops_gla_nccl_comm_abort(void* comm);
+TOPS_API int tops_gla_nccl_comm_check(void* comm);
+TOPS_API int tops_gla_state_exchange_wait(void* comm, void* stream, int32_t timeout_ms);
 
 /* ---- GLA layer pieces around the chunked op ------------ */
 

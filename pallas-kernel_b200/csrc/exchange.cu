@@ -13,8 +13,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "common.cuh"
 
@@ -27,6 +29,8 @@ struct Nccl {
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
   bool ok = false;
 };
 
@@ -42,7 +46,10 @@ static const Nccl& nccl() {
     n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     n.all_gather = reinterpret_cast<decltype(n.all_gather)>(dlsym(h, "ncclAllGather"));
     n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(h, "ncclGetErrorString"));
-    n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_gather && n.error_string;
+    n.comm_abort = reinterpret_cast<decltype(n.comm_abort)>(dlsym(h, "ncclCommAbort"));
+    n.async_error = reinterpret_cast<decltype(n.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_gather && n.error_string &&
+           n.comm_abort && n.async_error;
   });
   return n;
 }
@@ -115,6 +122,57 @@ TOPS_API int tops_gla_nccl_comm_destroy(void* comm) {
   if (comm == nullptr) return TOPS_OK;
   if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
   return nccl_status(nccl().comm_destroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy");
+}
+
+TOPS_API int tops_gla_nccl_comm_abort(void* comm) {
+  if (comm == nullptr) return TOPS_OK;
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  return nccl_status(nccl().comm_abort(static_cast<ncclComm_t>(comm)), "ncclCommAbort");
+}
+
+TOPS_API int tops_gla_nccl_comm_check(void* comm) {
+  TOPS_CHECK_ARG(comm != nullptr, "nccl_comm_check: comm is NULL");
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  ncclResult_t ar = ncclSuccess;
+  int rc = nccl_status(nccl().async_error(static_cast<ncclComm_t>(comm), &ar), "ncclCommGetAsyncError");
+  if (rc) return rc;
+  if (ar != ncclSuccess && ar != ncclInProgress) return nccl_status(ar, "NCCL communicator error");
+  return TOPS_OK;
+}
+
+TOPS_API int tops_gla_state_exchange_wait(void* comm, void* stream, int32_t timeout_ms) {
+  TOPS_CHECK_ARG(comm != nullptr && timeout_ms > 0, "state_exchange_wait: comm and a positive timeout are required");
+  if (!nccl().ok) return fail(TOPS_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) is not available");
+  cudaEvent_t ev = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  if (e != cudaSuccess) return cuda_status(e, "state_exchange_wait: event");
+  if ((e = cudaEventRecord(ev, static_cast<cudaStream_t>(stream))) != cudaSuccess) {
+    cudaEventDestroy(ev);
+    return cuda_status(e, "state_exchange_wait: record");
+  }
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  int rc = TOPS_OK;
+  for (;;) {
+    e = cudaEventQuery(ev);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      rc = cuda_status(e, "state_exchange_wait");
+      break;
+    }
+    if ((rc = tops_gla_nccl_comm_check(comm)) != TOPS_OK) {
+      nccl().comm_abort(static_cast<ncclComm_t>(comm));
+      break;
+    }
+    if (std::chrono::steady_clock::now() > deadline) {
+      nccl().comm_abort(static_cast<ncclComm_t>(comm));
+      rc = fail(TOPS_ERR_TIMEOUT, "state_exchange_wait: the exchange did not complete within " +
+                                      std::to_string(timeout_ms) + " ms; the communicator was aborted");
+      break;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+  cudaEventDestroy(ev);
+  return rc;
 }
 
 TOPS_API size_t tops_gla_state_exchange_workspace_size(const tops_gla_exchange_args* a) {

@@ -197,6 +197,19 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return r;
 }
 
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// a pair of 16-bit storage values (bf16, or fp16 when f16) packed from / widened to fp32
+__device__ __forceinline__ uint32_t pack16(float a, float b, bool f16) { return f16 ? pack_f16(a, b) : pack_bf16(a, b); }
+__device__ __forceinline__ float2 unpack16(uint32_t w, bool f16) {
+  if (f16) return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

@@ -133,6 +133,7 @@ struct PrepParams {
   int B, T, H, K, NTb;
   float scale;
   float* D;  // [B*NTb, H, K]
+  int f16;   // q, k stored as fp16 (bf16 otherwise); the gated copies are bf16 either way
 };
 
 struct PrepMaps {
@@ -291,11 +292,11 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
     uint32_t wqt[4][4], wkt[4][4], wqh[4][4], wkd[4][4];
 #pragma unroll
     for (int rr = 0; rr < 4; ++rr) {
-      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&xq[rr]);
-      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&xk[rr]);
+      const uint32_t* q2 = reinterpret_cast<const uint32_t*>(&xq[rr]);
+      const uint32_t* k2 = reinterpret_cast<const uint32_t*>(&xk[rr]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 fq = __bfloat1622float2(q2[e]), fk = __bfloat1622float2(k2[e]);
+        const float2 fq = ptx::unpack16(q2[e], p.f16), fk = ptx::unpack16(k2[e], p.f16);
         run[2 * e] += gv[rr][2 * e];
         run[2 * e + 1] += gv[rr][2 * e + 1];
         const float a0 = __expf(run[2 * e]), a1 = __expf(run[2 * e + 1]);
@@ -410,8 +411,8 @@ template <bool SEG>  // SEG: padded varlen problem, chunk ranges from p.blk_off
 __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMaps maps, ScanParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int nkb = p.K / 64;              // X tiles per chunk
-  const int nh = p.K / 128;              // state halves (TMEM lane blocks)
+  const int nh = (p.K + 127) / 128;      // state halves (TMEM lane blocks); K = 64 uses half of one
+  const int nkb = 2 * nh;                // X tiles per chunk (past K: zero-filled by the loads)
   const uint32_t buf_bytes = (uint32_t)(nkb + 2) * TILE_BYTES;
   unsigned char* stage_st = smem + 2 * buf_bytes;  // 8 warps x 2 slots x 2 KB
   __shared__ __align__(8) uint64_t bar_full[2], bar_mma;
@@ -430,6 +431,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   const int qd = warp & 3, hf = warp >> 2;  // lane quadrant, state half handled by this warp
   const int krow = hf * 128 + qd * 32 + lane;
   const bool active = hf < nh;
+  const bool krow_ok = krow < p.K;  // uniform per warp (K is a multiple of 64)
 
   if (warp == 0) {
     ptx::tmem_alloc(&tmem_base, 512);
@@ -473,7 +475,8 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[span_off + srow + cb * 32 + j] : 0.f;
+      for (int j = 0; j < 32; ++j)
+        r[j] = (p.init && krow_ok && v0 + cb * 32 + j < p.V) ? p.init[span_off + srow + cb * 32 + j] : 0.f;
       ptx::tmem_st32(tmem_lane_addr(sbuf(0), qd * 32, hf * 128 + cb * 32), r);
     }
     ptx::tmem_st_wait();
@@ -481,7 +484,8 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   bool ok = true;
   // the decay of chunk i+1 is fetched one iteration ahead (its latency hides behind chunk i)
   auto decay_of = [&](int i) {
-    return active && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
+    return active && krow_ok && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow)
+                                         : 1.f;
   };
   float d_next = decay_of(0), dprod = 1.f;
   for (int i = 0; i < n_it; ++i) {
@@ -540,6 +544,7 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
       const int rbase = (b * p.NTb + c) * p.H + h;
 #pragma unroll 1
       for (int cb = 0; cb < 4; ++cb) {
+        if (!krow_ok || v0 + cb * 32 >= p.V) continue;  // block past K or V (uniform per warp)
         float r[32];
         ptx::tmem_ld32(tmem_lane_addr(sbuf(i), qd * 32, hf * 128 + cb * 32), r);
         ptx::tmem_ld_wait();
@@ -563,12 +568,13 @@ __global__ void __launch_bounds__(256, 1) k_scan(const __grid_constant__ ScanMap
   }
   if (ok && (!SEG || n_it > 0)) ok = ptx::mbar_wait(&bar_mma, (uint32_t)((n_it - 1) & 1));
   ptx::tc_fence_after();
-  if (ok && active && p.span_decay && vt == 0)
+  if (ok && active && krow_ok && p.span_decay && vt == 0)
     p.span_decay[((size_t)(sp_ * p.B + b) * p.H + h) * p.K + krow] = dprod;
-  if (ok && active && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
+  if (ok && active && krow_ok && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
     const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
 #pragma unroll
     for (int cb = 0; cb < 4; ++cb) {
+      if (v0 + cb * 32 >= p.V) break;
       float r[32];
       ptx::tmem_ld32(tmem_lane_addr(sbuf(n_it), qd * 32, hf * 128 + cb * 32), r);
       ptx::tmem_ld_wait();
@@ -656,7 +662,7 @@ __global__ void __launch_bounds__(192, 1) k_out(const __grid_constant__ OutMaps 
   __shared__ __align__(8) uint64_t full[OUT_STAGES], empty[OUT_STAGES], accf[2], acce[2];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nvt = p.V / BV;
+  const int nvt = (p.V + BV - 1) / BV;
   const int items = p.B * p.NTb * p.H * nvt;
   const int nkb = p.K / 64 + 2;
 
@@ -827,7 +833,8 @@ struct FusedMaps {
   CUtensorMap y;   // fwd v, bwd do; [B,T,H,V] box (64,1,128,1)
   CUtensorMap ox;  // output-side x: fwd qhat, bwd kdec; box (64,1,128,1)
   CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1), bwd box (64,1,64,1)
-  bf16* out;       // output [B, T, H, V] bf16 (fwd o, bwd dv)
+  bf16* out;       // output [B, T, H, V] (fwd o, bwd dv): bf16, or fp16 when out_f16
+  int out_f16;
 };
 
 constexpr int FO_THREADS = 384;
@@ -841,8 +848,8 @@ template <bool SEG>
 __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constant__ FusedMaps maps, ScanParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int nh = p.K / 128;      // state halves
-  const int nxs = p.K / 128;     // output-side x stages per chunk (two 64-column tiles each)
+  const int nh = (p.K + 127) / 128;   // state halves; K = 64 uses half of one (loads past K read zeros)
+  const int nxs = nh;                 // output-side x stages per chunk (two 64-column tiles each)
   const int S = fo_stages(p.K);  // ring stages
   const uint32_t half_bytes = (uint32_t)p.K * 128;  // one 64-column half of the bf16 state copy
   unsigned char* hs = smem;                         // bf16 state copy: 2 halves [K rows][64 cols]
@@ -893,6 +900,7 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
   const int krow = hf * 128 + qd * 32 + lane;
   const bool pass_warp = warp >= 4;
   const bool active = pass_warp && hf < nh;
+  const bool krow_ok = krow < p.K;  // uniform per warp
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -902,7 +910,8 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
     for (int cb = 0; cb < 4; ++cb) {
       float r[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) r[j] = p.init ? p.init[span_off + srow + cb * 32 + j] : 0.f;
+      for (int j = 0; j < 32; ++j)
+        r[j] = (p.init && krow_ok && v0 + cb * 32 + j < p.V) ? p.init[span_off + srow + cb * 32 + j] : 0.f;
       ptx::tmem_st32(tmem_lane_addr(tmem_base, qd * 32, hf * 128 + cb * 32), r);
     }
     ptx::tmem_st_wait();
@@ -1046,11 +1055,12 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         float r[32];
         ptx::tmem_ld32(tmem_lane_addr(oacc(j), qd * 32, hf * 64 + cb * 32), r);
         ptx::tmem_ld_wait();
+        const bool f16 = maps.out_f16;
 #pragma unroll
         for (int j8 = 0; j8 < 4; ++j8)
           *reinterpret_cast<uint4*>(tile + ptx::sw128(t, cb * 64 + j8 * 16)) =
-              make_uint4(ptx::pack_bf16(r[j8 * 8 + 0], r[j8 * 8 + 1]), ptx::pack_bf16(r[j8 * 8 + 2], r[j8 * 8 + 3]),
-                         ptx::pack_bf16(r[j8 * 8 + 4], r[j8 * 8 + 5]), ptx::pack_bf16(r[j8 * 8 + 6], r[j8 * 8 + 7]));
+              make_uint4(ptx::pack16(r[j8 * 8 + 0], r[j8 * 8 + 1], f16), ptx::pack16(r[j8 * 8 + 2], r[j8 * 8 + 3], f16),
+                         ptx::pack16(r[j8 * 8 + 4], r[j8 * 8 + 5], f16), ptx::pack16(r[j8 * 8 + 6], r[j8 * 8 + 7], f16));
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -1059,7 +1069,7 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       for (int it = 0; it < 8; ++it) {
         const int rr = qd * 32 + 4 * it + (lane >> 3), row = c * BT + rr;
         const uint4 x = *reinterpret_cast<const uint4*>(tile + ptx::sw128(rr, (lane & 7) * 16));
-        if (row < p.T)
+        if (row < p.T && v0 + hf * 64 < p.V)
           *reinterpret_cast<uint4*>(maps.out + (((size_t)b * p.T + row) * p.H + h) * p.V + v0 + hf * 64 +
                                     (lane & 7) * 8) = x;
       }
@@ -1068,7 +1078,9 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       if (lane == 0) ptx::mbar_arrive(&y_empty[j & 1]);
     };
     auto decay_of = [&](int i) {
-      return active && i < n_it ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow) : 1.f;
+      return active && krow_ok && i < n_it
+                 ? __ldg(p.D + ((size_t)(b * p.NTb + chunk_of(i)) * p.H + h) * p.K + krow)
+                 : 1.f;
     };
     bool ok = true;
     float d_next = decay_of(0);
@@ -1111,7 +1123,8 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         for (int it = 0; it < 16; ++it) {
           const int r = hf * 128 + qd * 32 + 2 * it + (lane >> 4);
           const uint4 x = *reinterpret_cast<const uint4*>(hs + hb * half_bytes + ptx::sw128(r, c16 * 16));
-          *reinterpret_cast<uint4*>(p.states + (rbase + r) * p.V + v0 + hb * 64 + c16 * 8) = x;
+          if (r < p.K && v0 + hb * 64 < p.V)
+            *reinterpret_cast<uint4*>(p.states + (rbase + r) * p.V + v0 + hb * 64 + c16 * 8) = x;
         }
       }
       if (i > 0) epilogue(i - 1);
@@ -1121,10 +1134,11 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
       ptx::tc_fence_after();
       if (ok) epilogue(n_it - 1);
     }
-    if (ok && active && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
+    if (ok && active && krow_ok && p.fin && (p.fin_mode == 0 || sp_ == p.nspan - 1)) {
       const size_t srow = ((size_t)(sq * p.H + h) * p.K + krow) * p.V + v0 + (p.fin_mode == 0 ? span_off : 0);
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
+        if (v0 + cb * 32 >= p.V) break;
         float r[32];
         ptx::tmem_ld32(tmem_lane_addr(tmem_base, qd * 32, hf * 128 + cb * 32), r);
         ptx::tmem_ld_wait();
@@ -1162,6 +1176,7 @@ struct DqkParams {
   int B, T, H, K, V, NTb;
   float scale;
   bf16* dq; bf16* dk; float* dg;
+  int f16;  // q, k, dq, dk stored as fp16 (do, v and the states are bf16 either way)
 };
 
 struct DqkMaps {
@@ -1219,7 +1234,7 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
   const int k0 = kt * 64, row0 = c * BT;
   const int srow = (b * p.NTb + c) * p.H + h;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nvb = p.V / 64;  // even: V is a multiple of 128
+  const int nvb = p.V < 128 ? 2 : p.V / 64;  // even: V is 64 (second block read as zeros) or a multiple of 128
 
   if (warp == 0) {
     ptx::tmem_alloc(&tmem_base, 256);
@@ -1406,13 +1421,13 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
       uint4* pq = reinterpret_cast<uint4*>(qtl + ptx::sw128(row, chunk * 16));
       uint4* pk = reinterpret_cast<uint4*>(ktl + ptx::sw128(row, chunk * 16));
       uint4 xq = *pq, xk = *pk;
-      __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&xq);
-      __nv_bfloat162* k2 = reinterpret_cast<__nv_bfloat162*>(&xk);
+      uint32_t* q2 = reinterpret_cast<uint32_t*>(&xq);
+      uint32_t* k2 = reinterpret_cast<uint32_t*>(&xk);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 fq = __bfloat1622float2(q2[e]), fk = __bfloat1622float2(k2[e]);
-        q2[e] = __floats2bfloat162_rn(fq.x * __expf(x8[2 * e]), fq.y * __expf(x8[2 * e + 1]));
-        k2[e] = __floats2bfloat162_rn(fk.x * __expf(-x8[2 * e]), fk.y * __expf(-x8[2 * e + 1]));
+      for (int e = 0; e < 4; ++e) {  // raw q, k (bf16 or fp16) -> bf16 q~, k~
+        const float2 fq = ptx::unpack16(q2[e], p.f16), fk = ptx::unpack16(k2[e], p.f16);
+        q2[e] = ptx::pack_bf16(fq.x * __expf(x8[2 * e]), fq.y * __expf(x8[2 * e + 1]));
+        k2[e] = ptx::pack_bf16(fk.x * __expf(-x8[2 * e]), fk.y * __expf(-x8[2 * e + 1]));
       }
       *pq = xq;
       *pk = xk;
@@ -1501,8 +1516,8 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
       uint32_t dqw[8], dkw[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        dqw[u] = ptx::pack_bf16(m4[2 * u], m4[2 * u + 1]);
-        dkw[u] = ptx::pack_bf16(m5[2 * u], m5[2 * u + 1]);
+        dqw[u] = ptx::pack16(m4[2 * u], m4[2 * u + 1], p.f16);
+        dkw[u] = ptx::pack16(m5[2 * u], m5[2 * u + 1], p.f16);
       }
       *reinterpret_cast<uint4*>(qtl + qb) = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
       *reinterpret_cast<uint4*>(qtl + qb2) = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
@@ -1599,7 +1614,7 @@ struct Spans {
   int n, len;
 };
 static Spans spans_for(const tops_gla_shape& s, int NTb) {
-  const int units = (s.V / BV) * s.H * s.B;
+  const int units = ((s.V + BV - 1) / BV) * s.H * s.B;
   const int nsm = sm_count();
   Spans r{1, NTb};
   if (units * 2 > nsm || NTb < 16) return r;
@@ -1650,9 +1665,14 @@ static tops_gla_shape padded_shape(const tops_gla_shape& s) {
   return p;
 }
 
+// K = 64 and V = 64 run as one 128-wide state tile whose upper half is padding: the loads past
+// K or V read zeros (TMA fills out-of-bounds boxes), so the padded state rows / columns stay
+// zero, and every store, decay read and initial / final state access is guarded to the real
+// extent (as the reference pads K and V to 128, tops/ops/gla/chunk.py:1128-1132).
 bool eligible(const tops_gla_shape& s) {
-  if (!(s.dtype == TOPS_BF16 && (s.K == 128 || s.K == 256) && s.V % BV == 0 && s.T > 0 && s.B > 0 && s.H > 0))
-    return false;
+  const bool kok = s.K == 64 || s.K == 128 || s.K == 256;
+  const bool vok = s.V == 64 || (s.V > 0 && s.V % BV == 0);
+  if (!((s.dtype == TOPS_BF16 || s.dtype == TOPS_F16) && kok && vok && s.T > 0 && s.B > 0 && s.H > 0)) return false;
   // packed varlen: only while the block padding at most doubles the rows (long segments)
   if (s.cu_seqlens != nullptr && (s.B != 1 || s.N <= 0 || (size_t)varlen_rows(s) > 2 * (size_t)s.T + BT)) return false;
   return tops_gla_has_tcgen05() && encode_fn() != nullptr;
@@ -1723,6 +1743,7 @@ static int pad_rows(const void* src, void* dst, size_t row_bytes, int rows, cons
 // Intermediates of the forward that the backward reuses (one contiguous block).
 struct Saved {
   bf16 *qh, *kd, *A, *h;
+  bf16* vb = nullptr;  // fp16 problems: bf16 copy of v (an MMA operand of the scans and of k_dqk)
   float* D;
   SpanBufs sb;  // scratch of a span-split forward scan (empty when the scan runs in one span)
 };
@@ -1745,6 +1766,7 @@ static size_t carve_saved(const tops_gla_shape& s, void* base, Saved* sv, bool s
   v.A = reinterpret_cast<bf16*>(take(tok * BT * 2));
   v.D = reinterpret_cast<float*>(take((size_t)s.B * NTb * s.H * s.K * 4));
   v.h = reinterpret_cast<bf16*>(take((size_t)s.B * NTb * s.H * s.K * s.V * 2));
+  if (s.dtype == TOPS_F16) v.vb = reinterpret_cast<bf16*>(take(tok * s.V * 2));
   if (spans) off = carve_spans(s, spans_for(s, NTb), static_cast<char*>(base), off, &v.sb, force_spans);
   if (sv) *sv = v;
   return off;
@@ -1772,7 +1794,7 @@ static int scan_spans_zero(const tops_gla_shape& s, const ScanMaps& sm, int reve
   if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
   LaunchTimer lt(st, reverse ? "tc_scan_bwd_span" : "tc_scan_span");
   ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, nullptr, sb.E, nullptr, spn.n, spn.len, 0, sb.P, nullptr};
-  k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+  k_scan<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
   TOPS_CUDA_LAUNCH_CHECK("tc_scan_span");
   return TOPS_OK;
 }
@@ -1798,9 +1820,9 @@ static int scan_spans_finish(const tops_gla_shape& s, const ScanMaps& sm, int re
   LaunchTimer lt(st, name);
   ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, span_init, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
   if (fm)
-    k_scan_out<false><<<dim3(s.V / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+    k_scan_out<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
   else
-    k_scan<false><<<dim3(s.V / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
+    k_scan<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
   TOPS_CUDA_LAUNCH_CHECK(name);
   return TOPS_OK;
 }
@@ -1820,10 +1842,10 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, blk_off};
     if (fm) {
       if ((e = set_smem(k_scan_out<true>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
-      k_scan_out<true><<<dim3(s.V / BV, s.H, s.N), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+      k_scan_out<true><<<dim3((s.V + BV - 1) / BV, s.H, s.N), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
     } else {
       if ((e = set_smem(k_scan<true>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
-      k_scan<true><<<dim3(s.V / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
+      k_scan<true><<<dim3((s.V + BV - 1) / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
     }
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
@@ -1832,9 +1854,9 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, nullptr};
     if (fm)
-      k_scan_out<false><<<dim3(s.V / BV, s.H, s.B), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+      k_scan_out<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
     else
-      k_scan<false><<<dim3(s.V / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
+      k_scan<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
     return TOPS_OK;
   }
@@ -1852,13 +1874,46 @@ static bool fused_out() {
   return on;
 }
 
+// fp16 -> bf16 copy (8 elements per thread and step): the operands that feed tcgen05 MMAs next
+// to bf16 intermediates (v, do) must be bf16 themselves, since one MMA takes one operand type.
+__global__ void k_f16_to_bf16(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n8) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 x = src[i];
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = ptx::unpack16(w[e], true);
+      o[e] = ptx::pack_bf16(f.x, f.y);
+    }
+    dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+static int to_bf16(const void* src, bf16* dst, size_t n, cudaStream_t st) {
+  const size_t n8 = n / 8;  // token tensors hold a multiple of 64 elements per row
+  if (n8 == 0) return TOPS_OK;
+  LaunchTimer lt(st, "tc_f16_to_bf16");
+  const size_t blocks = (n8 + 255) / 256 < (size_t)sm_count() * 8 ? (n8 + 255) / 256 : (size_t)sm_count() * 8;
+  k_f16_to_bf16<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst), n8);
+  TOPS_CUDA_LAUNCH_CHECK("tc f16 to bf16");
+  return TOPS_OK;
+}
+
+// storage type of q, k, o, dq, dk, dv for the tensor maps
+static CUtensorMapDataType io_type(const tops_gla_shape& s) {
+  return s.dtype == TOPS_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
 // Tensor maps of k_prep (q, k, g in; qhat, kdec, A out) and of the forward state scan
 // (kdec, v in; chunk states out) over the saved block `sv`.
 static bool fwd_maps(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
                      const Saved& sv, PrepMaps* pm, ScanMaps* sm) {
   const int NTb = (s.T + BT - 1) / BT;
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  return map_tok(&pm->q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&pm->k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+  const CUtensorMapDataType IO = io_type(s);
+  if (sv.vb != nullptr) v = sv.vb;  // fp16 problem: the scans read the bf16 copy of v
+  return map_tok(&pm->q, q, IO, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&pm->k, k, IO, 2, s.B, s.T, s.H, s.K, 64, BT) &&
          map_tok(&pm->g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
          map_tok(&pm->qh, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
          map_tok(&pm->kd, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
@@ -1872,7 +1927,7 @@ static int launch_prep(const tops_gla_shape& s, const PrepMaps& pm, const Saved&
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   LaunchTimer lt(st, "tc_prep");
-  PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
+  PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D, s.dtype == TOPS_F16};
   if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
   if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
     return cuda_status(e, "tc prep carveout");
@@ -1891,12 +1946,15 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   carve_saved(s, saved, &sv, blk_off == nullptr);
   const int NTb = (s.T + BT - 1) / BT;
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const void* fv = v;  // the caller's v (fp16 problems convert it into sv.vb first)
   PrepMaps pm;
   ScanMaps sm;
   bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm);
+  if (sv.vb != nullptr) v = sv.vb;
   OutMaps om;
   FusedMaps fm;
-  const bool fused = o != nullptr && fused_out();
+  // fp16 runs the fused kernel only (its epilogue writes fp16; k_out stores bf16 through TMA)
+  const bool fused = o != nullptr && (fused_out() || s.dtype == TOPS_F16);
   if (o != nullptr && !fused)
     okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
@@ -1908,10 +1966,12 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
           map_tok(&fm.ox, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
   fm.out = static_cast<bf16*>(o);
+  fm.out_f16 = s.dtype == TOPS_F16;
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd: cuTensorMapEncodeTiled failed (alignment?)");
   cudaError_t e;
-  int rc = launch_prep(s, pm, sv, st);
-  if (rc) return rc;
+  int rc;
+  if (sv.vb != nullptr && (rc = to_bf16(fv, sv.vb, (size_t)s.B * s.T * s.H * s.V, st))) return rc;
+  if ((rc = launch_prep(s, pm, sv, st))) return rc;
   rc = run_scan(s, sm, 0, sv.D, h0, ht, sv.h, sv.sb, spans_for(s, NTb), st, fused ? "tc_scan_out" : "tc_scan",
                     blk_off, fused ? &fm : nullptr);
   if (rc) return rc;
@@ -1920,7 +1980,7 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     LaunchTimer lt(st, "tc_out");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 0, static_cast<bf16*>(o)};
     if ((e = set_smem(k_out, out_smem())) != cudaSuccess) return cuda_status(e, "tc out attr");
-    const int items = s.B * NTb * s.H * (s.V / BV);
+    const int items = s.B * NTb * s.H * ((s.V + BV - 1) / BV);
     const int grid = items < sm_count() ? items : sm_count();
     k_out<<<grid, 192, out_smem(), st>>>(om, op);
     TOPS_CUDA_LAUNCH_CHECK("tc_out");
@@ -1929,6 +1989,11 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
 }
 
 static size_t dqk_smem() { return 2 * (size_t)DQK_STG + 1024; }
+
+// fp16 problems: bytes of the bf16 copy of do in the backward workspace (0 otherwise)
+static size_t dob_bytes(const tops_gla_shape& s) {
+  return s.dtype == TOPS_F16 ? (((size_t)s.B * s.T * s.H * s.V * 2 + 1023) & ~size_t(1023)) : 0;
+}
 
 // reverse scan: qhat (saved) and do in, chunk-end state gradients dh out
 static bool bwd_scan_maps(const tops_gla_shape& s, const void* dO, const Saved& sv, bf16* dhs, ScanMaps* sm) {
@@ -1943,6 +2008,7 @@ static bool bwd_scan_maps(const tops_gla_shape& s, const void* dO, const Saved& 
 static bool bwd_fused_maps(const tops_gla_shape& s, const void* dO, void* dv, const Saved& sv, FusedMaps* fm) {
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   fm->out = static_cast<bf16*>(dv);
+  fm->out_f16 = s.dtype == TOPS_F16;
   return map_tok(&fm->sx, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
          map_tok(&fm->y, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
          map_tok(&fm->ox, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
@@ -1953,19 +2019,22 @@ static bool dqk_maps(const tops_gla_shape& s, const void* q, const void* k, cons
                      const void* dO, const Saved& sv, bf16* dhs, void* dq, void* dk, float* dg, DqkMaps* dm) {
   const int NTb = (s.T + BT - 1) / BT;
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapDataType IO = io_type(s);
+  if (sv.vb != nullptr) v = sv.vb;  // fp16: v and do are read as bf16 copies (dO is the copy already)
   return map_tok(&dm->dO, dO, BF, 2, s.B, s.T, s.H, s.V, 64, BT) && map_tok(&dm->v, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
          map_state(&dm->hs, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
          map_state(&dm->dhs, dhs, s.B * NTb * s.H, s.K, s.V, 64) &&
          map_tok(&dm->g, g, F32, 4, s.B, s.T, s.H, s.K, 32, BT) && map_tok(&dm->dg, dg, F32, 4, s.B, s.T, s.H, s.K, 32, BT) &&
-         map_tok(&dm->q, q, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->k, k, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-         map_tok(&dm->dq, dq, BF, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->dk, dk, BF, 2, s.B, s.T, s.H, s.K, 64, BT);
+         map_tok(&dm->q, q, IO, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->k, k, IO, 2, s.B, s.T, s.H, s.K, 64, BT) &&
+         map_tok(&dm->dq, dq, IO, 2, s.B, s.T, s.H, s.K, 64, BT) && map_tok(&dm->dk, dk, IO, 2, s.B, s.T, s.H, s.K, 64, BT);
 }
 
 static int launch_dqk(const tops_gla_shape& s, const DqkMaps& dm, void* dq, void* dk, float* dg, cudaStream_t st) {
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   LaunchTimer lt(st, "tc_dqk");
-  DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
+  DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg,
+               s.dtype == TOPS_F16};
   if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
   // two CTAs per SM need the largest shared-memory carveout
   if ((e = cudaFuncSetAttribute(k_dqk, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
@@ -1980,6 +2049,7 @@ static size_t bwd_core_workspace(const tops_gla_shape& s, bool have_saved, bool 
   const int NTb = (s.T + BT - 1) / BT;
   size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);  // dh states
   if (spans) n = (carve_spans(s, spans_for(s, NTb), nullptr, n, nullptr) + 1023) & ~size_t(1023);
+  n += dob_bytes(s);
   if (!have_saved) n += carve_saved(s, nullptr, nullptr, spans);
   return n;
 }
@@ -1996,11 +2066,16 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   const Spans spn = blk_off ? Spans{1, NTb} : spans_for(s, NTb);
   SpanBufs sb;
   const size_t span_end = (carve_spans(s, spn, ws, dh_bytes, &sb) + 1023) & ~size_t(1023);
+  bf16* dob = dob_bytes(s) ? reinterpret_cast<bf16*>(ws + span_end) : nullptr;
   void* saved = const_cast<void*>(saved_in);
   int rc;
   if (saved == nullptr) {  // recompute the forward intermediates (o is discarded into dv's buffer)
-    saved = ws + span_end;
+    saved = ws + span_end + dob_bytes(s);
     if ((rc = fwd_core(s, q, k, v, g, h0, dv, nullptr, saved, st, blk_off))) return rc;
+  }
+  if (dob != nullptr) {  // fp16: do feeds MMAs beside bf16 operands, so it is read as a bf16 copy
+    if ((rc = to_bf16(dO, dob, (size_t)s.B * s.T * s.H * s.V, st))) return rc;
+    dO = dob;
   }
   Saved sv;
   carve_saved(s, saved, &sv, blk_off == nullptr);
@@ -2014,7 +2089,7 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   }
   OutMaps om;
   FusedMaps fm;
-  const bool fused = fused_out();
+  const bool fused = fused_out() || s.dtype == TOPS_F16;
   if (fused)
     okm = okm && bwd_fused_maps(s, dO, dv, sv, &fm);
   else
@@ -2033,7 +2108,7 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     LaunchTimer lt(st, "tc_out_dv");
     OutParams op{s.B, s.T, s.H, s.K, s.V, NTb, 1, static_cast<bf16*>(dv)};
     if ((e = set_smem(k_out, out_smem())) != cudaSuccess) return cuda_status(e, "tc out attr");
-    const int items = s.B * NTb * s.H * (s.V / BV);
+    const int items = s.B * NTb * s.H * ((s.V + BV - 1) / BV);
     const int grid = items < sm_count() ? items : sm_count();
     k_out<<<grid, 192, out_smem(), st>>>(om, op);
     TOPS_CUDA_LAUNCH_CHECK("tc_out_dv");
@@ -2073,6 +2148,7 @@ int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const 
   if (!fwd_maps(s, q, k, v, g, sv, &pm, &sm)) return fail(TOPS_ERR_CUDA, "tc fwd span: cuTensorMapEncodeTiled failed");
   const Spans spn = spans_of(s);
   int rc;
+  if (sv.vb != nullptr && (rc = to_bf16(v, sv.vb, (size_t)s.B * s.T * s.H * s.V, st))) return rc;
   if ((rc = launch_prep(s, pm, sv, st)) || (rc = scan_spans_zero(s, sm, 0, sv.D, sv.sb, spn, st))) return rc;
   return span_total(s, spn, sv.sb, local_state, decay, st);
 }
@@ -2086,10 +2162,11 @@ int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const
   FusedMaps fm;
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm) && map_tok(&fm.sx, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
-                   map_tok(&fm.y, v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
+                   map_tok(&fm.y, sv.vb ? sv.vb : v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
                    map_tok(&fm.ox, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
                    map_tok(&fm.a, sv.A, BF, 2, s.B, s.T, s.H, BT, 64, BT);
   fm.out = static_cast<bf16*>(o);
+  fm.out_f16 = s.dtype == TOPS_F16;
   if (!okm) return fail(TOPS_ERR_CUDA, "tc fwd span: cuTensorMapEncodeTiled failed");
   return scan_spans_finish(s, sm, 0, sv.D, h_in, ht, sv.h, sv.sb, spans_of(s), st, "tc_scan_out", &fm);
 }
@@ -2098,15 +2175,17 @@ int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const
 size_t bwd_span_workspace(const tops_gla_shape& s) {
   const int NTb = (s.T + BT - 1) / BT;
   const size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
-  return (carve_spans(s, spans_of(s), nullptr, n, nullptr, true) + 1023) & ~size_t(1023);
+  return ((carve_spans(s, spans_of(s), nullptr, n, nullptr, true) + 1023) & ~size_t(1023)) + dob_bytes(s);
 }
 
-static void carve_bwd_span(const tops_gla_shape& s, void* workspace, bf16** dhs, SpanBufs* sb) {
+// dh states, span scratch and (fp16) the bf16 copy of do, which the first phase converts
+static void carve_bwd_span(const tops_gla_shape& s, void* workspace, bf16** dhs, SpanBufs* sb, bf16** dob) {
   const int NTb = (s.T + BT - 1) / BT;
   char* ws = static_cast<char*>(workspace);
   *dhs = reinterpret_cast<bf16*>(ws);
   const size_t n = ((size_t)s.B * NTb * s.H * s.K * s.V * 2 + 1023) & ~size_t(1023);
-  carve_spans(s, spans_of(s), ws, n, sb, true);
+  const size_t end = (carve_spans(s, spans_of(s), ws, n, sb, true) + 1023) & ~size_t(1023);
+  *dob = dob_bytes(s) ? reinterpret_cast<bf16*>(ws + end) : nullptr;
 }
 
 int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, void* workspace, float* local_dh0,
@@ -2114,12 +2193,18 @@ int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, v
   Saved sv;
   carve_saved(s, const_cast<void*>(saved), &sv, true, true);
   bf16* dhs;
+  bf16* dob;
   SpanBufs sb;
-  carve_bwd_span(s, workspace, &dhs, &sb);
+  carve_bwd_span(s, workspace, &dhs, &sb, &dob);
+  int rc;
+  if (dob != nullptr) {
+    if ((rc = to_bf16(dO, dob, (size_t)s.B * s.T * s.H * s.V, st))) return rc;
+    dO = dob;
+  }
   ScanMaps sm;
   if (!bwd_scan_maps(s, dO, sv, dhs, &sm)) return fail(TOPS_ERR_CUDA, "tc bwd span: cuTensorMapEncodeTiled failed");
   const Spans spn = spans_of(s);
-  int rc = scan_spans_zero(s, sm, 1, sv.D, sb, spn, st);
+  rc = scan_spans_zero(s, sm, 1, sv.D, sb, spn, st);
   return rc ? rc : span_total(s, spn, sb, local_dh0, nullptr, st);
 }
 
@@ -2129,8 +2214,10 @@ int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const
   Saved sv;
   carve_saved(s, const_cast<void*>(saved), &sv, true, true);
   bf16* dhs;
+  bf16* dob;
   SpanBufs sb;
-  carve_bwd_span(s, workspace, &dhs, &sb);
+  carve_bwd_span(s, workspace, &dhs, &sb, &dob);
+  if (dob != nullptr) dO = dob;  // converted by the first phase
   ScanMaps sm;
   FusedMaps fm;
   DqkMaps dm;

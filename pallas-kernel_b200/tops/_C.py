@@ -125,6 +125,9 @@ SIGNATURES = {
     "tops_gla_nccl_get_unique_id": (C.c_int, [VP]),
     "tops_gla_nccl_comm_init": (C.c_int, [C.POINTER(C.c_void_p), I32, VP, I32]),
     "tops_gla_nccl_comm_destroy": (C.c_int, [VP]),
+    "tops_gla_nccl_comm_abort": (C.c_int, [VP]),
+    "tops_gla_nccl_comm_check": (C.c_int, [VP]),
+    "tops_gla_state_exchange_wait": (C.c_int, [VP, VP, I32]),
     "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),

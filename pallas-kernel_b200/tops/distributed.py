@@ -25,6 +25,8 @@ defaults use this library's kernels.
 from __future__ import annotations
 
 import ctypes
+import threading
+import time
 from typing import Callable
 
 import torch
@@ -32,19 +34,97 @@ import torch.distributed as dist
 
 __all__ = ["shard", "prefix_states", "suffix_grads", "all_gather_stack", "seq_parallel_forward",
            "seq_parallel_backward", "seq_parallel_forward_phased", "seq_parallel_backward_phased",
-           "chunk_gla_seq_parallel", "NcclStateExchange"]
+           "chunk_gla_seq_parallel", "NcclStateExchange", "PeerWatchdog", "PeerLostError"]
+
+
+class PeerLostError(RuntimeError):
+    """A rank of the group left, crashed or stalled: detected on the host before a collective."""
+
+
+class PeerWatchdog:
+    """Host-side liveness of every rank of a group, through the group's key-value store.
+
+    A daemon thread publishes this rank's heartbeat (a counter) every ``interval`` seconds and
+    reads the other ranks'.  A peer whose heartbeat has not advanced for ``timeout`` seconds,
+    that announced it left (:meth:`close`), or whose store became unreachable marks the group
+    lost; :meth:`check` (no I/O) then raises :class:`PeerLostError`.  The exchange calls it
+    before it launches a collective, so a rank never enqueues NCCL work that would wait on
+    the GPU for a peer that is gone.  ``store`` defaults to the default process group's store.
+    """
+
+    def __init__(self, store=None, rank=None, world=None, timeout: float = 30.0, interval: float = 0.2,
+                 prefix: str = "tops_gla/heartbeat"):
+        if store is None:
+            store = dist.distributed_c10d._get_default_store()
+        self.store = dist.PrefixStore(prefix, store)
+        self.rank = dist.get_rank() if rank is None else rank
+        self.world = dist.get_world_size() if world is None else world
+        self.timeout, self.interval = float(timeout), float(interval)
+        self.lost: str | None = None
+        self._stop = threading.Event()
+        now = time.monotonic()
+        self._last = {r: None for r in range(self.world) if r != self.rank}
+        self._seen = {r: now for r in self._last}
+        self.store.set(str(self.rank), "0")
+        self._thread = threading.Thread(target=self._run, name="tops-gla-peer-watchdog", daemon=True)
+        self._thread.start()
+
+    def _poll(self, beat: int) -> None:
+        self.store.set(str(self.rank), str(beat))
+        now = time.monotonic()
+        for r in self._last:
+            key = str(r)
+            v = self.store.get(key) if self.store.check([key]) else None
+            if v == b"left":
+                self.lost = f"rank {r} left the group"
+            elif v is not None and v != self._last[r]:
+                self._last[r], self._seen[r] = v, now
+            elif now - self._seen[r] > self.timeout:
+                self.lost = f"rank {r} sent no heartbeat for {now - self._seen[r]:.1f} s"
+
+    def _run(self) -> None:
+        beat = 1
+        while not self._stop.wait(self.interval) and self.lost is None:
+            try:
+                self._poll(beat)
+            except Exception as e:  # the store itself is gone (its host rank died)
+                self.lost = f"the group's store is unreachable ({type(e).__name__}: {e})"
+            beat += 1
+
+    def check(self) -> None:
+        """Raise PeerLostError if a peer is known to be gone (no I/O)."""
+        if self.lost is not None:
+            raise PeerLostError(f"rank {self.rank}: {self.lost}")
+
+    def close(self) -> None:
+        """Stop the thread and tell the other ranks that this one leaves."""
+        self._stop.set()
+        self._thread.join(timeout=max(1.0, 5 * self.interval))
+        try:
+            self.store.set(str(self.rank), "left")
+        except Exception:
+            pass
 
 
 class NcclStateExchange:
     """The C ABI's state exchange (``tops_gla_state_exchange``: one ncclAllGather of the
     packed (state, decay) pairs and one prefix / suffix kernel) on a communicator of this
     library's own; ``group`` only broadcasts NCCL's unique id.  Every rank of the group must
-    construct it (communicator creation is collective)."""
+    construct it (communicator creation is collective).
 
-    def __init__(self, group=None):
+    Failure handling: with ``liveness_timeout`` (seconds; None turns it off) a
+    :class:`PeerWatchdog` tracks the other ranks on the host, and every exchange first checks
+    it: if a peer left or stalled, the communicator is aborted (``tops_gla_nccl_comm_abort``,
+    which does not wait for peers) and :class:`PeerLostError` is raised before any NCCL work is
+    enqueued.  :meth:`wait` bounds the host's wait for an exchange already launched."""
+
+    _made = 0
+
+    def __init__(self, group=None, liveness_timeout: float | None = 30.0):
         from . import _C
         self._C = _C
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.watchdog = None
         idbuf = (ctypes.c_char * 128)()
         if self.rank == 0:
             _C.call("tops_gla_nccl_get_unique_id", ctypes.addressof(idbuf))
@@ -53,9 +133,40 @@ class NcclStateExchange:
         ctypes.memmove(idbuf, obj[0], 128)
         self.comm = ctypes.c_void_p()
         _C.call("tops_gla_nccl_comm_init", ctypes.byref(self.comm), self.world, ctypes.addressof(idbuf), self.rank)
+        NcclStateExchange._made += 1  # the same count on every rank: construction is collective
+        if liveness_timeout is not None and group is None:
+            self.watchdog = PeerWatchdog(timeout=liveness_timeout, prefix=f"tops_gla/exchange{NcclStateExchange._made}")
+
+    def check_peers(self) -> None:
+        """Raise PeerLostError (after aborting the communicator) if a peer is gone."""
+        if self.watchdog is None:
+            return
+        try:
+            self.watchdog.check()
+        except PeerLostError:
+            self.abort()
+            raise
+
+    def abort(self) -> None:
+        """Abort the communicator without waiting for peers (the handle is freed)."""
+        if self.comm:
+            self._C.lib().tops_gla_nccl_comm_abort(self.comm)
+            self.comm = ctypes.c_void_p()
+        if self.watchdog is not None:
+            self.watchdog.close()
+            self.watchdog = None
+
+    def wait(self, timeout_s: float, stream=None) -> None:
+        """Wait on the host, at most ``timeout_s``, for the exchanges enqueued so far; on an NCCL
+        error or at the deadline the communicator is aborted and TopsError is raised."""
+        st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        self._C.call("tops_gla_state_exchange_wait", self.comm, st, max(1, int(timeout_s * 1000)))
 
     def _run(self, backward: bool, local: torch.Tensor, decay: torch.Tensor, boundary, want_total: bool):
         C = self._C
+        self.check_peers()
+        if not self.comm:
+            raise PeerLostError("the exchange's communicator was aborted")
         local = local.float().contiguous()
         decay = decay.float().contiguous()
         boundary = None if boundary is None else boundary.float().contiguous()
@@ -82,6 +193,9 @@ class NcclStateExchange:
         if self.comm:
             self._C.call("tops_gla_nccl_comm_destroy", self.comm)
             self.comm = ctypes.c_void_p()
+        if self.watchdog is not None:
+            self.watchdog.close()
+            self.watchdog = None
 
 
 def shard(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:

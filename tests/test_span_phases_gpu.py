@@ -108,7 +108,7 @@ def test_span_entry_points_reject_what_they_do_not_serve(env):
     _C, _core, _ = env
     import ctypes
     L = _C.lib()
-    q = torch.zeros(1, 256, 2, 64, dtype=torch.bfloat16, device="cuda")  # K = 64: CUDA-core path
+    q = torch.zeros(1, 256, 2, 32, dtype=torch.bfloat16, device="cuda")  # K = 32: CUDA-core path
     plan = _core.make_plan(q, 64, 64, None, None)
     assert L.tops_gla_chunk_span_saved_size(ctypes.byref(plan.shape())) == 0
     a = _C.ChunkFwdArgs(plan.shape(), 1, 1, 1, 1, None, 1, None, None, None, None, None, 0, 1, 1 << 30)
