@@ -133,13 +133,13 @@ struct PrepParams {
   int B, T, H, K, NTb;
   float scale;
   float* D;  // [B*NTb, H, K]
-  int f16;   // q, k stored as fp16 (bf16 otherwise); the gated copies are bf16 either way
 };
 
 struct PrepMaps {
   CUtensorMap q, k, g, qh, kd, A;
 };
 
+template <bool F16>  // q, k stored as fp16 (bf16 otherwise); the gated copies are bf16 either way
 __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMaps maps, PrepParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(256, 2) k_prep(const __grid_constant__ PrepMap
       const uint32_t* k2 = reinterpret_cast<const uint32_t*>(&xk[rr]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 fq = ptx::unpack16(q2[e], p.f16), fk = ptx::unpack16(k2[e], p.f16);
+        const float2 fq = ptx::unpack16(q2[e], F16), fk = ptx::unpack16(k2[e], F16);
         run[2 * e] += gv[rr][2 * e];
         run[2 * e + 1] += gv[rr][2 * e + 1];
         const float a0 = __expf(run[2 * e]), a1 = __expf(run[2 * e + 1]);
@@ -834,24 +834,27 @@ struct FusedMaps {
   CUtensorMap ox;  // output-side x: fwd qhat, bwd kdec; box (64,1,128,1)
   CUtensorMap a;   // A [B,T,H,128]: fwd box (64,1,128,1), bwd box (64,1,64,1)
   bf16* out;       // output [B, T, H, V] (fwd o, bwd dv): bf16, or fp16 when out_f16
-  int out_f16;
+  int out_f16;     // selects the k_scan_out instantiation
 };
 
 constexpr int FO_THREADS = 384;
 constexpr uint32_t FO_STAGE = 2 * TILE_BYTES;  // 32 KB
 __host__ __device__ constexpr int fo_stages(int K) { return K == 256 ? 3 : 4; }
+// shared memory of k_scan_out: the bf16 state copy (K padded to whole 128-row state halves),
+// two y slots and the ring
 static size_t fo_smem(int K) {
-  return (size_t)K * 256 + 2 * (size_t)FO_STAGE + (size_t)fo_stages(K) * FO_STAGE + 1024;
+  const size_t Kp = (size_t)(K + 127) / 128 * 128;
+  return Kp * 256 + 2 * (size_t)FO_STAGE + (size_t)fo_stages(K) * FO_STAGE + 1024;
 }
 
-template <bool SEG>
+template <bool SEG, bool F16>  // F16: the output (o / dv) is stored as fp16, bf16 otherwise
 __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constant__ FusedMaps maps, ScanParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nh = (p.K + 127) / 128;   // state halves; K = 64 uses half of one (loads past K read zeros)
   const int nxs = nh;                 // output-side x stages per chunk (two 64-column tiles each)
   const int S = fo_stages(p.K);  // ring stages
-  const uint32_t half_bytes = (uint32_t)p.K * 128;  // one 64-column half of the bf16 state copy
+  const uint32_t half_bytes = (uint32_t)nh * 128 * 128;  // one 64-column half of the bf16 state copy (padded K rows)
   unsigned char* hs = smem;                         // bf16 state copy: 2 halves [K rows][64 cols]
   unsigned char* yslot0 = smem + 2 * half_bytes;    // 2 slots x [128 rows][128 cols] (two 16 KB tiles)
   unsigned char* ring = yslot0 + 2 * FO_STAGE;
@@ -1055,7 +1058,7 @@ __global__ void __launch_bounds__(FO_THREADS, 1) k_scan_out(const __grid_constan
         float r[32];
         ptx::tmem_ld32(tmem_lane_addr(oacc(j), qd * 32, hf * 64 + cb * 32), r);
         ptx::tmem_ld_wait();
-        const bool f16 = maps.out_f16;
+        constexpr bool f16 = F16;
 #pragma unroll
         for (int j8 = 0; j8 < 4; ++j8)
           *reinterpret_cast<uint4*>(tile + ptx::sw128(t, cb * 64 + j8 * 16)) =
@@ -1176,7 +1179,6 @@ struct DqkParams {
   int B, T, H, K, V, NTb;
   float scale;
   bf16* dq; bf16* dk; float* dg;
-  int f16;  // q, k, dq, dk stored as fp16 (do, v and the states are bf16 either way)
 };
 
 struct DqkMaps {
@@ -1218,6 +1220,7 @@ __device__ __forceinline__ float dqk_reduce16(const float (&v)[16], int lane) {
   return r1 + __shfl_xor_sync(0xffffffffu, r1, 1);
 }
 
+template <bool F16>  // q, k, dq, dk stored as fp16 (do, v and the states are bf16 either way)
 __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps maps, DqkParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1425,7 +1428,7 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
       uint32_t* k2 = reinterpret_cast<uint32_t*>(&xk);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {  // raw q, k (bf16 or fp16) -> bf16 q~, k~
-        const float2 fq = ptx::unpack16(q2[e], p.f16), fk = ptx::unpack16(k2[e], p.f16);
+        const float2 fq = ptx::unpack16(q2[e], F16), fk = ptx::unpack16(k2[e], F16);
         q2[e] = ptx::pack_bf16(fq.x * __expf(x8[2 * e]), fq.y * __expf(x8[2 * e + 1]));
         k2[e] = ptx::pack_bf16(fk.x * __expf(-x8[2 * e]), fk.y * __expf(-x8[2 * e + 1]));
       }
@@ -1516,8 +1519,8 @@ __global__ void __launch_bounds__(256, 2) k_dqk(const __grid_constant__ DqkMaps 
       uint32_t dqw[8], dkw[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        dqw[u] = ptx::pack16(m4[2 * u], m4[2 * u + 1], p.f16);
-        dkw[u] = ptx::pack16(m5[2 * u], m5[2 * u + 1], p.f16);
+        dqw[u] = ptx::pack16(m4[2 * u], m4[2 * u + 1], F16);
+        dkw[u] = ptx::pack16(m5[2 * u], m5[2 * u + 1], F16);
       }
       *reinterpret_cast<uint4*>(qtl + qb) = make_uint4(dqw[0], dqw[1], dqw[2], dqw[3]);
       *reinterpret_cast<uint4*>(qtl + qb2) = make_uint4(dqw[4], dqw[5], dqw[6], dqw[7]);
@@ -1808,7 +1811,8 @@ static int scan_spans_finish(const tops_gla_shape& s, const ScanMaps& sm, int re
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
-  if (fm && (e = set_smem(k_scan_out<false>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
+  const auto kso = fm && fm->out_f16 ? k_scan_out<false, true> : k_scan_out<false, false>;
+  if (fm && (e = set_smem(kso, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
   const float* span_init = init;
   if (spn.n > 1) {
     LaunchTimer lt(st, "tc_span_prefix");
@@ -1820,7 +1824,7 @@ static int scan_spans_finish(const tops_gla_shape& s, const ScanMaps& sm, int re
   LaunchTimer lt(st, name);
   ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, span_init, fin, states, spn.n, spn.len, 1, nullptr, nullptr};
   if (fm)
-    k_scan_out<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+    kso<<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
   else
     k_scan<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B * spn.n), 256, scan_smem(s.K), st>>>(sm, sp);
   TOPS_CUDA_LAUNCH_CHECK(name);
@@ -1836,13 +1840,15 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   if ((e = set_smem(k_scan<false>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
-  if (fm && (e = set_smem(k_scan_out<false>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
+  const auto kso = fm && fm->out_f16 ? k_scan_out<false, true> : k_scan_out<false, false>;
+  const auto kso_seg = fm && fm->out_f16 ? k_scan_out<true, true> : k_scan_out<true, false>;
+  if (fm && (e = set_smem(kso, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
   if (blk_off != nullptr) {  // padded varlen problem: one CTA column per segment
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, blk_off};
     if (fm) {
-      if ((e = set_smem(k_scan_out<true>, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
-      k_scan_out<true><<<dim3((s.V + BV - 1) / BV, s.H, s.N), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+      if ((e = set_smem(kso_seg, fo_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan_out attr");
+      kso_seg<<<dim3((s.V + BV - 1) / BV, s.H, s.N), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
     } else {
       if ((e = set_smem(k_scan<true>, scan_smem(s.K))) != cudaSuccess) return cuda_status(e, "tc scan attr");
       k_scan<true><<<dim3((s.V + BV - 1) / BV, s.H, s.N), 256, scan_smem(s.K), st>>>(sm, sp);
@@ -1854,7 +1860,7 @@ static int run_scan(const tops_gla_shape& s, const ScanMaps& sm, int reverse, co
     LaunchTimer lt(st, name);
     ScanParams sp{s.B, s.T, s.H, s.K, s.V, NTb, reverse, D, init, fin, states, 1, NTb, 0, nullptr, nullptr};
     if (fm)
-      k_scan_out<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
+      kso<<<dim3((s.V + BV - 1) / BV, s.H, s.B), FO_THREADS, fo_smem(s.K), st>>>(*fm, sp);
     else
       k_scan<false><<<dim3((s.V + BV - 1) / BV, s.H, s.B), 256, scan_smem(s.K), st>>>(sm, sp);
     TOPS_CUDA_LAUNCH_CHECK(name);
@@ -1927,12 +1933,13 @@ static int launch_prep(const tops_gla_shape& s, const PrepMaps& pm, const Saved&
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   LaunchTimer lt(st, "tc_prep");
-  PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D, s.dtype == TOPS_F16};
-  if ((e = set_smem(k_prep, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
-  if ((e = cudaFuncSetAttribute(k_prep, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+  PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
+  auto kern = s.dtype == TOPS_F16 ? k_prep<true> : k_prep<false>;
+  if ((e = set_smem(kern, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
     return cuda_status(e, "tc prep carveout");
   const int items = NTb * s.H * s.B;
-  k_prep<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
+  kern<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
   TOPS_CUDA_LAUNCH_CHECK("tc_prep");
   return TOPS_OK;
 }
@@ -1952,7 +1959,7 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm);
   if (sv.vb != nullptr) v = sv.vb;
   OutMaps om;
-  FusedMaps fm;
+  FusedMaps fm{};
   // fp16 runs the fused kernel only (its epilogue writes fp16; k_out stores bf16 through TMA)
   const bool fused = o != nullptr && (fused_out() || s.dtype == TOPS_F16);
   if (o != nullptr && !fused)
@@ -2033,13 +2040,13 @@ static int launch_dqk(const tops_gla_shape& s, const DqkMaps& dm, void* dq, void
   const int NTb = (s.T + BT - 1) / BT;
   cudaError_t e;
   LaunchTimer lt(st, "tc_dqk");
-  DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg,
-               s.dtype == TOPS_F16};
-  if ((e = set_smem(k_dqk, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
+  DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
+  auto kern = s.dtype == TOPS_F16 ? k_dqk<true> : k_dqk<false>;
+  if ((e = set_smem(kern, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
   // two CTAs per SM need the largest shared-memory carveout
-  if ((e = cudaFuncSetAttribute(k_dqk, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
+  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
     return cuda_status(e, "tc dqk carveout");
-  k_dqk<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
+  kern<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
   TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
   return TOPS_OK;
 }
@@ -2088,7 +2095,7 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
     return run_scan(s, sm, 1, sv.D, dht, dh0, nullptr, sb, spn, st, "tc_scan_bwd", blk_off);
   }
   OutMaps om;
-  FusedMaps fm;
+  FusedMaps fm{};
   const bool fused = fused_out() || s.dtype == TOPS_F16;
   if (fused)
     okm = okm && bwd_fused_maps(s, dO, dv, sv, &fm);
@@ -2159,7 +2166,7 @@ int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const
   carve_saved(s, saved, &sv, true, true);
   PrepMaps pm;
   ScanMaps sm;
-  FusedMaps fm;
+  FusedMaps fm{};
   const CUtensorMapDataType BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const bool okm = fwd_maps(s, q, k, v, g, sv, &pm, &sm) && map_tok(&fm.sx, sv.kd, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
                    map_tok(&fm.y, sv.vb ? sv.vb : v, BF, 2, s.B, s.T, s.H, s.V, 64, BT) &&
@@ -2219,7 +2226,7 @@ int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const
   carve_bwd_span(s, workspace, &dhs, &sb, &dob);
   if (dob != nullptr) dO = dob;  // converted by the first phase
   ScanMaps sm;
-  FusedMaps fm;
+  FusedMaps fm{};
   DqkMaps dm;
   const bool okm = bwd_scan_maps(s, dO, sv, dhs, &sm) && bwd_fused_maps(s, dO, dv, sv, &fm) &&
                    dqk_maps(s, q, k, v, g, dO, sv, dhs, dq, dk, dg, &dm);
