@@ -420,6 +420,9 @@ def run_ours(args):
     else:
         strong["note"] = "at one GPU the strong-scaling legs are the headline (config 3) and decode (config 2)"
 
+    # ---- K = V = 64 heads: tensor-core path next to the CUDA-core kernels ----------------
+    h64 = head64_bench(args, world, rank, dev)
+
     # ---- config-5 model training step (GLA layers + SwiGLU, data parallel) -----------
     torch.cuda.empty_cache()
     lm = None if args.no_model else model_bench(args, world, rank, local, dev)
@@ -440,7 +443,7 @@ def run_ours(args):
                            "parallelism": f"batch x heads shards, {world} GPU(s), no collective",
                            "l2": "inputs (537 MB/step) larger than L2; no flush"},
                 "roofline": roof, "step_roofline": step_roof, "decode": dec, "long_context": lc,
-                "strong_scaling": strong, "model_dp": lm,
+                "strong_scaling": strong, "head64": h64, "model_dp": lm,
                 "e2e": e2e,
                 "gpu_launches": int(launches), "clocks": clocks, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
@@ -618,6 +621,122 @@ def strong_cfg3_bench(args, world, rank, dev):
                                             "chunk_size": C, "inputs_bytes_per_gpu": B * T * H * (6 * K + 4 * V)}}
 
 
+def head64_bench(args, world, rank, dev):
+    """K = V = 64 heads (the size the reference's tests use, which it pads to 128) on the
+    tensor-core path, timed next to the CUDA-core kernels on the same inputs: chunk_gla fwd+bwd,
+    B=4, T=4096, H=16, bf16.  The CUDA-core path is selected through the same C ABI by asking
+    for the sub-function intermediates (g_cumsum, A, h), which only it returns."""
+    import torch
+
+    from tops import _C
+    from tops.ops.gla import _core
+    B, T, H, K, V, C = 4, 4096, 16, 64, 64, 64
+    gen = torch.Generator(device=dev).manual_seed(64 + rank)
+    bf = torch.bfloat16
+    q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
+    do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    plan = _core.make_plan(q, V, C, None, K ** -0.5)
+    assert _core.saved_size(plan, g) > 0
+
+    def tc_step():
+        o, _, sv = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+        return _core.chunk_bwd(plan, q, k, v, g, None, do, None, block=sv.get("block"))
+
+    gc = torch.empty(B, T, H, K, dtype=torch.float32, device=dev)
+    A = torch.empty(B, T, H, C, dtype=torch.float32, device=dev)
+    h = torch.empty(plan.NT, H, K, V, dtype=torch.float32, device=dev)
+    o = torch.empty(B, T, H, V, dtype=bf, device=dev)
+    fa = _C.ChunkFwdArgs(plan.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), None, _C.ptr(o), None,
+                         _C.ptr(gc), _C.ptr(A), _C.ptr(h), None, 0, None, 0)
+    fws = torch.empty(max(int(_C.lib().tops_gla_chunk_fwd_workspace_size(fa)), 1), dtype=torch.uint8, device=dev)
+    fa.workspace, fa.workspace_bytes = _C.ptr(fws), fws.numel()
+    grads = [torch.empty_like(x) for x in (q, k, v)] + [torch.empty_like(g)]
+    ba = _C.ChunkBwdArgs(plan.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), None, _C.ptr(do), None,
+                         _C.ptr(gc), _C.ptr(A), _C.ptr(h), *(_C.ptr(x) for x in grads), None, None, 0, None, 0)
+    bws = torch.empty(max(int(_C.lib().tops_gla_chunk_bwd_workspace_size(ba)), 1), dtype=torch.uint8, device=dev)
+    ba.workspace, ba.workspace_bytes = _C.ptr(bws), bws.numel()
+
+    def simt_step():
+        st = _C.stream_of(q)
+        _C.call("tops_gla_chunk_fwd", fa, st)
+        _C.call("tops_gla_chunk_bwd", ba, st)
+
+    out = {}
+    for name, fn in (("tensor_core", tc_step), ("cuda_core", simt_step)):
+        for _ in range(3):
+            fn()
+        steps = max(3, min(args.steps, 10))
+        barrier(world)
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            fn()
+        e1.record(s)
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        out[name] = {"ms_per_step": ms, "tokens_per_s": B * T * world / (ms * 1e-3)}
+    out["speedup_tensor_core"] = out["cuda_core"]["ms_per_step"] / out["tensor_core"]["ms_per_step"]
+    out["config"] = {"B_per_gpu": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "dtype": "bf16",
+                     "workload": "chunk_gla fwd+bwd at K = V = 64"}
+    return out
+
+
+def op_only(args):
+    """One small case of a named op, run a few times: the command the per-kernel ncu summaries
+    of the kernels outside the config-3 step (recurrence backward, CUDA-core chunk kernels,
+    layer kernels) are taken from."""
+    import torch
+
+    from tops.ops.gla import _core
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    bf = torch.bfloat16
+    if args.op == "recurrent_bwd":  # BASELINE config 2's shapes over T = 64 steps, B = 32
+        B, T, H, K, V = 32, 64, 16, 128, 128
+        q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
+        v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+        gk = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
+        h0 = torch.randn(B, H, K, V, device=dev, generator=gen) * 0.1
+        do = torch.randn(B, T, H, V, device=dev, generator=gen)
+        o, _ = _core.recurrent_fwd(q, k, v, gk, None, h0, K ** -0.5, False, False, None, B)
+
+        def run():
+            return _core.recurrent_bwd(q, k, v, gk, None, h0, o, do, None, K ** -0.5, False, None, B)
+    elif args.op == "simt_chunk":  # fp32 chunk_gla fwd+bwd (CUDA-core kernels), config-1 layout scaled up
+        B, T, H, K, V, C = 4, 2048, 4, 64, 64, 64
+        q, k = (torch.randn(B, T, H, K, device=dev, generator=gen) for _ in range(2))
+        v = torch.randn(B, T, H, V, device=dev, generator=gen)
+        g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
+        do = torch.randn(B, T, H, V, device=dev, generator=gen)
+        plan = _core.make_plan(q, V, C, None, K ** -0.5)
+
+        def run():
+            o, _, sv = _core.chunk_fwd(plan, q, k, v, g, None, False, save=True)
+            return _core.chunk_bwd(plan, q, k, v, g, None, do, None, sv.get("g_cumsum"), sv.get("A"), sv.get("h"))
+    elif args.op == "layer":  # the GLA layer's fused kernels: gate logsigmoid and RMSNorm x swish gate
+        import tops.layers as L
+        cfg = L.GLAConfig()
+        with torch.device(dev):
+            layer = L.GatedLinearAttention(hidden_size=cfg.hidden_size, num_heads=cfg.num_heads, expand_k=0.5,
+                                           expand_v=1.0, mode="chunk", layer_idx=0).to(bf)
+        x = torch.randn(4, 2048, cfg.hidden_size, device=dev, generator=gen).to(bf).requires_grad_()
+
+        def run():
+            y = layer(x)[0]
+            y.float().sum().backward()
+    else:
+        raise SystemExit(f"unknown --op {args.op}")
+    for _ in range(max(args.steps, 1)):
+        run()
+    torch.cuda.synchronize()
+    print(json.dumps({"op": args.op, "ok": True}), flush=True)
+    return 0
+
+
 def model_bench(args, world, rank, local, dev):
     """Config 5: one training step (forward, next-token loss, backward, gradient all-reduce
     when N>1, fp32-master AdamW) of the 24-layer GLA + SwiGLU model on synthetic tokens
@@ -711,11 +830,15 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="only the config-2 decode leg (for ncu captures)")
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the timed fwd+bwd loop (no decode / e2e / CPU legs); for ncu launch lists")
+    ap.add_argument("--op", choices=("recurrent_bwd", "simt_chunk", "layer"), default=None,
+                    help="run only a small case of one op --steps times (for ncu captures of its kernels)")
     args = ap.parse_args()
     if args.batch is not None:
         CFG3["B"] = int(args.batch)
     if args.impl == "reference":
         return run_reference(args)
+    if args.op is not None:
+        return op_only(args)
     return run_ours(args)
 
 

@@ -79,7 +79,7 @@ def test_f16_matches_bf16_path_on_shared_values(env):
     q, k, v, g, h0, do, _ = _inputs(3, B, T, H, K, V, torch.bfloat16)
     outs = {}
     for dt in (torch.bfloat16, torch.float16):
-        qt, kt, vt = (x.to(dt).requires_grad_() for x in (q, k, v))
+        qt, kt, vt = (x.detach().to(dt).clone().requires_grad_() for x in (q, k, v))
         gt = g.clone().requires_grad_()
         o, ht = G.chunk_gla(qt, kt, vt, gt, initial_state=h0, output_final_state=True, chunk_size=C)
         (o.float() * do.float()).sum().backward()
