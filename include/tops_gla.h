@@ -119,7 +119,7 @@ typedef struct tops_gla_chunk_fwd_args {
   float* h;                    /* [NT,H,K,V] */
   void* workspace; size_t workspace_bytes;
   /* Opaque block receiving what the backward reuses when the forward runs on the
-   * tensor-core path (bf16, K in {128, 256}, V % 128 == 0, fixed length); size from
+   * tensor-core path (bf16 or fp16, K in {64, 128, 256}, V = 64 or a multiple of 128); size from
    * tops_gla_chunk_saved_size(), NULL = do not save.  Pass it to the backward. */
   void* saved; size_t saved_bytes;
 } tops_gla_chunk_fwd_args;
@@ -275,8 +275,8 @@ TOPS_API int tops_gla_state_combine(int32_t N, int32_t H, int32_t K, int32_t V, 
 /* ---- sequence-parallel forward / backward in two phases ---
  * No reference counterpart (the reference has no multi-device code); the math is the
  * linear decomposition of its chunked scan (tops/ops/common/chunk_h.py:372-386).  Each rank
- * holds one contiguous span of a long sequence (fixed length, tensor-core path: bf16,
- * K in {128, 256}, V % 128 == 0).  The scan is linear in the span's incoming state, so the
+ * holds one contiguous span of a long sequence (fixed length, tensor-core path: bf16 or fp16,
+ * K in {64, 128, 256}, V = 64 or a multiple of 128).  The scan is linear in the span's incoming state, so the
  * first phase does all the work that does not depend on it and returns the span's own
  * final state from a zero state (local_state [N,H,K,V] fp32) and its total decay
  * (decay [N,H,K] fp32, exp of the span's gate sums); the host exchanges these between ranks
