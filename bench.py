@@ -695,8 +695,9 @@ def op_only(args):
     torch.cuda.set_device(0)
     gen = torch.Generator(device=dev).manual_seed(9)
     bf = torch.bfloat16
-    if args.op == "recurrent_bwd":  # BASELINE config 2's shapes over T = 64 steps, B = 32
-        B, T, H, K, V = 32, 64, 16, 128, 128
+    # sizes: each case's tensors exceed the 126 MB L2 and stay a few hundred MB in all
+    if args.op == "recurrent_bwd":  # BASELINE config 2's head shape over T = 64 steps, B = 64
+        B, T, H, K, V = 64, 64, 16, 128, 128
         q, k = (torch.randn(B, T, H, K, device=dev, generator=gen).to(bf) for _ in range(2))
         v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
         gk = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
@@ -707,7 +708,7 @@ def op_only(args):
         def run():
             return _core.recurrent_bwd(q, k, v, gk, None, h0, o, do, None, K ** -0.5, False, None, B)
     elif args.op == "simt_chunk":  # fp32 chunk_gla fwd+bwd (CUDA-core kernels), config-1 layout scaled up
-        B, T, H, K, V, C = 4, 2048, 4, 64, 64, 64
+        B, T, H, K, V, C = 8, 4096, 4, 64, 64, 64
         q, k = (torch.randn(B, T, H, K, device=dev, generator=gen) for _ in range(2))
         v = torch.randn(B, T, H, V, device=dev, generator=gen)
         g = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
