@@ -100,16 +100,28 @@ k_fwd_h(tops_gla_shape sh, const T* __restrict__ k, const T* __restrict__ v, con
     }
     for (int j0 = s; j0 < e; j0 += TILE) {
       const int L = min(TILE, e - j0);
-      for (int i = tid; i < TILE * TILE; i += NTHREADS) {
-        const int j = i / TILE, c = i % TILE;
-        float kv = 0.f, vv = 0.f;
+      // every global load of the tile first, then the arithmetic: the loads of one thread's
+      // 16 elements are in flight together instead of one dependent round trip each
+      constexpr int PER = TILE * TILE / NTHREADS;
+      float lk[PER], lg[PER], lv[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int i = tid + u * NTHREADS, j = i / TILE, c = i % TILE;
+        lk[u] = 0.f;
+        lg[u] = 0.f;
+        lv[u] = 0.f;
         if (j < L && k0 + c < K) {
           const size_t o = tok(j0 + j, h, H, K, k0 + c);
-          kv = to_f(k[o]) * expf(gl[c] - gc[o]);
+          lk[u] = to_f(k[o]);
+          lg[u] = gc[o];
         }
-        if (j < L && v0 + c < V) vv = to_f(v[tok(j0 + j, h, H, V, v0 + c)]);
-        kd[j][c] = kv;
-        vs[j][c] = vv;
+        if (j < L && v0 + c < V) lv[u] = to_f(v[tok(j0 + j, h, H, V, v0 + c)]);
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int i = tid + u * NTHREADS, j = i / TILE, c = i % TILE;
+        kd[j][c] = (j < L && k0 + c < K) ? lk[u] * expf(gl[c] - lg[u]) : 0.f;
+        vs[j][c] = lv[u];
       }
       __syncthreads();
       for (int j = 0; j < L; ++j) {
@@ -187,16 +199,27 @@ k_bwd_dh(tops_gla_shape sh, const T* __restrict__ q, const float* __restrict__ g
     }
     for (int j0 = s; j0 < e; j0 += TILE) {
       const int L = min(TILE, e - j0);
-      for (int x = tid; x < TILE * TILE; x += NTHREADS) {
-        const int j = x / TILE, c = x % TILE;
-        float qv = 0.f, dv = 0.f;
+      // every global load of the tile first, then the arithmetic (loads in flight together)
+      constexpr int PER = TILE * TILE / NTHREADS;
+      float lq[PER], lg[PER], ld[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int x = tid + u * NTHREADS, j = x / TILE, c = x % TILE;
+        lq[u] = 0.f;
+        lg[u] = 0.f;
+        ld[u] = 0.f;
         if (j < L && k0 + c < K) {
           const size_t o = tok(j0 + j, h, H, K, k0 + c);
-          qv = to_f(q[o]) * expf(gc[o]) * scale;
+          lq[u] = to_f(q[o]);
+          lg[u] = gc[o];
         }
-        if (j < L && v0 + c < V) dv = to_f(dO[tok(j0 + j, h, H, V, v0 + c)]);
-        qh[j][c] = qv;
-        ds[j][c] = dv;
+        if (j < L && v0 + c < V) ld[u] = to_f(dO[tok(j0 + j, h, H, V, v0 + c)]);
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int x = tid + u * NTHREADS, j = x / TILE, c = x % TILE;
+        qh[j][c] = (j < L && k0 + c < K) ? lq[u] * expf(lg[u]) * scale : 0.f;
+        ds[j][c] = ld[u];
       }
       __syncthreads();
       for (int j = 0; j < L; ++j) {
