@@ -150,3 +150,15 @@ def test_xla_custom_call_failure_reaches_the_status(lib, tmp_path):
         getattr(L, name)(None, ctypes.cast(arr, ctypes.c_void_p), b"\x00" * 7, 7, ctypes.cast(st, ctypes.c_void_p))
         assert st.raw[0] == 1, name
         assert b"bad descriptor" in st.raw, st.raw[:80]
+
+
+def test_nccl_failure_entry_points_validate_without_a_device(lib):
+    """Abort of a NULL communicator is a no-op; the check and the bounded wait reject a NULL
+    communicator or a non-positive timeout before touching NCCL or the device."""
+    L = lib.lib()
+    assert L.tops_gla_nccl_comm_abort(None) == 0
+    assert L.tops_gla_nccl_comm_check(None) == -1
+    assert b"comm is NULL" in L.tops_gla_last_error()
+    assert L.tops_gla_state_exchange_wait(None, None, 100) == -1
+    assert L.tops_gla_state_exchange_wait(1, None, 0) == -1
+    assert b"positive timeout" in L.tops_gla_last_error()

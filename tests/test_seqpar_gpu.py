@@ -63,6 +63,9 @@ def _worker(rank, world, port, out, use_exchange=False):
     o, ht = TD.chunk_gla_seq_parallel(qs, ks, vs, gs, initial_state=h0r, chunk_size=64, exchange=ex)
     loss = (o.float() * do[:, sl].float()).sum() + (ht * dht).sum()  # ht and dht are replicated
     loss.backward()
+    if ex is not None:  # the bounded host wait returns once the exchanges are done; no peer is lost
+        ex.wait(30.0)
+        ex.check_peers()
     res = dict(o=o.detach().cpu(), ht=ht.detach().cpu(), dq=qs.grad.cpu(), dk=ks.grad.cpu(), dv=vs.grad.cpu(),
                dg=gs.grad.cpu())
     if rank == 0:

@@ -86,3 +86,35 @@ def test_f16_matches_bf16_path_on_shared_values(env):
         outs[dt] = (o.float(), ht, qt.grad.float(), kt.grad.float(), vt.grad.float(), gt.grad)
     for nm, a, b in zip(("o", "ht", "dq", "dk", "dv", "dg"), outs[torch.float16], outs[torch.bfloat16]):
         assert_rel_l2(f"{nm} fp16 vs bf16", a, b, 5e-3)  # outputs rounded to fp16 vs bf16 at the end
+
+
+@pytest.mark.parametrize("K,V", [(64, 64), (64, 256), (256, 64)], ids=["k64v64", "k64v256", "k256v64"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_tc_varlen_head_sizes(env, K, V, dtype):
+    """Packed varlen (cu_seqlens, a one-token segment among them) on the tensor-core path with
+    padded head sizes and fp16: segments are padded to 128-row blocks on the device, the scans
+    follow the segment boundaries; forward + backward against the oracle per the same values."""
+    _C, _core, G = env
+    cu = [0, 300, 301, 777, 1000]
+    T, N, H, C = cu[-1], len(cu) - 1, 2, 64
+    q, k, v, g, _, do, _ = _inputs(K + V, 1, T, H, K, V, dtype)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    h0 = torch.randn(N, H, K, V, device="cuda", generator=gen) * 0.1
+    dht = torch.randn(N, H, K, V, device="cuda", generator=gen) * 0.1
+    cut = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    plan = _core.make_plan(q, V, C, cut, K ** -0.5)
+    assert _core.saved_size(plan, g) > 0, "expected the tensor-core path"
+    qt, kt, vt, gt = (x.clone().requires_grad_() for x in (q, k, v, g))
+    h0t = h0.clone().requires_grad_()
+    o, ht = G.chunk_gla(qt, kt, vt, gt, initial_state=h0t, output_final_state=True, cu_seqlens=cut, chunk_size=C)
+    ((o.float() * do.float()).sum() + (ht * dht).sum()).backward()
+    torch.cuda.synchronize()
+    assert _C.lib().tops_gla_device_error() == 0
+    qn, kn, vn, gn, h0n, don, dhtn = (x.float().cpu().numpy() for x in (q, k, v, g, h0, do, dht))
+    o_r, ht_r = O.chunk_gla(qn, kn, vn, gn, initial_state=h0n, output_final_state=True, cu_seqlens=cu, chunk_size=C)
+    dq_r, dk_r, dv_r, dg_r, dh0_r = O.chunk_gla_bwd(qn, kn, vn, gn, None, K ** -0.5, h0n, None, None, don, dhtn,
+                                                    cu, C)
+    for nm, got, ref in (("o", o, o_r), ("ht", ht, ht_r), ("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r),
+                         ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r), ("dh0", h0t.grad, dh0_r)):
+        assert_rel_l2(nm, got, ref, TOL)
+        assert_max_rel(nm, got, ref, TOL)
