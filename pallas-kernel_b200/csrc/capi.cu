@@ -373,12 +373,19 @@ int32_t tops_gla_timing_collect(char* names, int32_t name_stride, float* ms, int
 int32_t tops_gla_abi_version(void) { return TOPS_GLA_ABI_VERSION; }
 
 int32_t tops_gla_has_tcgen05(void) {
+  static std::atomic<int> cache[64] = {};  // per device: 0 unknown, 1 no, 2 yes
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c != 0) return c == 2 ? 1 : 0;
+  }
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
   if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return 0;
-  return (major == 10 && minor == 0) ? 1 : 0;
+  const int32_t yes = (major == 10 && minor == 0) ? 1 : 0;
+  if (dev >= 0 && dev < 64) cache[dev].store(yes ? 2 : 1, std::memory_order_relaxed);
+  return yes;
 }
 
 int32_t tops_gla_num_chunks(int32_t B, int32_t T, int32_t C, const int32_t* cu, int32_t N, int32_t* offs) {

@@ -33,8 +33,10 @@
 // swizzle that TMA writes and the UMMA descriptors describe.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -1601,10 +1603,18 @@ int selftest_wait_timeout(cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // host orchestration
 // ---------------------------------------------------------------------------
+// SM count of the current device, looked up once per device
 static int sm_count() {
-  int dev = 0, n = 148;
+  static std::atomic<int> cache[64] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 148;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -1783,9 +1793,29 @@ static size_t prep_smem() { return 6 * TILE_BYTES + 1024; }
 static size_t scan_smem(int K) { return 2 * (size_t)(K / 64 + 2) * TILE_BYTES + 8 * 2 * 2048 + 1024; }
 static size_t out_smem() { return (size_t)OUT_STAGES * STAGE_BYTES + 2 * TILE_BYTES + 1024; }
 
+// Dynamic shared memory limit of a kernel, set once per (device, kernel, size): the launches of
+// a step then issue no attribute calls (host time that counts when a rank's step is short).
 template <typename KernelT>
 static cudaError_t set_smem(KernelT k, size_t bytes) {
-  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  struct Entry {
+    int dev;
+    const void* fn;
+    size_t bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* fn = reinterpret_cast<const void*>(k);
+  std::lock_guard<std::mutex> lk(mu);
+  for (const Entry& e : done)
+    if (e.dev == dev && e.fn == fn && e.bytes >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  // the largest shared-memory carveout: every kernel here keeps big tiles in shared memory
+  // (k_prep and k_dqk need it for two CTAs per SM)
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess) done.push_back({dev, fn, bytes});
+  return e;
 }
 
 // First launch of a span-split scan: every span from a zero state, its final state into
@@ -1936,8 +1966,6 @@ static int launch_prep(const tops_gla_shape& s, const PrepMaps& pm, const Saved&
   PrepParams pp{s.B, s.T, s.H, s.K, NTb, s.scale, sv.D};
   auto kern = s.dtype == TOPS_F16 ? k_prep<true> : k_prep<false>;
   if ((e = set_smem(kern, prep_smem())) != cudaSuccess) return cuda_status(e, "tc prep attr");
-  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
-    return cuda_status(e, "tc prep carveout");
   const int items = NTb * s.H * s.B;
   kern<<<items < 2 * sm_count() ? items : 2 * sm_count(), 256, prep_smem(), st>>>(pm, pp);
   TOPS_CUDA_LAUNCH_CHECK("tc_prep");
@@ -2043,9 +2071,6 @@ static int launch_dqk(const tops_gla_shape& s, const DqkMaps& dm, void* dq, void
   DqkParams dp{s.B, s.T, s.H, s.K, s.V, NTb, s.scale, static_cast<bf16*>(dq), static_cast<bf16*>(dk), dg};
   auto kern = s.dtype == TOPS_F16 ? k_dqk<true> : k_dqk<false>;
   if ((e = set_smem(kern, dqk_smem())) != cudaSuccess) return cuda_status(e, "tc dqk attr");
-  // two CTAs per SM need the largest shared-memory carveout
-  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100)) != cudaSuccess)
-    return cuda_status(e, "tc dqk carveout");
   kern<<<dim3(s.K / 64, NTb, s.B * s.H), 256, dqk_smem(), st>>>(dm, dp);
   TOPS_CUDA_LAUNCH_CHECK("tc_dqk");
   return TOPS_OK;
