@@ -1619,7 +1619,8 @@ static int sm_count() {
 }
 
 // Span split of the state scans: enough spans that the scan grid fills the SMs (one CTA
-// per SM: 512 TMEM columns), at least 8 chunks per span; one span when the (batch, head,
+// per SM: 512 TMEM columns), at least 4 chunks per span (config 3 at one sequence per GPU:
+// 8 spans, 0.225 ms per fwd+bwd step against 0.260 with 4); one span when the (batch, head,
 // V-tile) units alone fill half the GPU or the sequence is short.  A split runs every chunk
 // twice (the zero-state pass, which has no output GEMM, then the re-scan), in exchange for a
 // chain of NTb / spans chunks per CTA instead of NTb.
@@ -1630,9 +1631,9 @@ static Spans spans_for(const tops_gla_shape& s, int NTb) {
   const int units = ((s.V + BV - 1) / BV) * s.H * s.B;
   const int nsm = sm_count();
   Spans r{1, NTb};
-  if (units * 2 > nsm || NTb < 16) return r;
+  if (units * 2 > nsm || NTb < 8) return r;
   int S = nsm / units;
-  if (S > NTb / 8) S = NTb / 8;
+  if (S > NTb / 4) S = NTb / 4;
   if (S < 2) return r;
   r.len = (NTb + S - 1) / S;
   r.n = (NTb + r.len - 1) / r.len;
