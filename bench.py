@@ -736,7 +736,7 @@ def op_only(args):
         v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
         gk = (torch.nn.functional.logsigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)) / 16).contiguous()
         h0 = torch.randn(B, H, K, V, device=dev, generator=gen) * 0.1
-        do = torch.randn(B, T, H, V, device=dev, generator=gen)
+        do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)  # the C ABI reads do in q's dtype
         o, _ = _core.recurrent_fwd(q, k, v, gk, None, h0, K ** -0.5, False, False, None, B)
 
         def run():

@@ -202,9 +202,21 @@ int fwd(const tops_gla_recurrent_args& a, cudaStream_t st);
 }  // namespace decode
 namespace rec {
 
-size_t fwd_workspace(const tops_gla_recurrent_args& a) {
-  int rows, splits;
+// The forward over T > 1 steps splits K over more CTAs for the same reason as the backward
+// (4 rows per warp; the partial outputs are summed by k_sum_splits): B64 T64 H16 K=V=128
+// 1.59 -> 0.76 ms, B16 T256 1.79 -> 0.99 ms.  A decode step (T = 1) runs the decode kernel.
+static void fwd_plan(const tops_gla_recurrent_args& a, int& rows, int& splits) {
   plan(a.K, rows, splits);
+  if (a.T > 1 && rows > 4) {
+    rows = 4;
+    splits = ceil_div(a.K, rows * WARPS);
+  }
+}
+
+size_t fwd_workspace(const tops_gla_recurrent_args& a) {
+  if (decode::supported(a)) return 0;
+  int rows, splits;
+  fwd_plan(a, rows, splits);
   if (splits <= 1) return 0;
   return (size_t)splits * a.B * a.T * a.H * a.V * sizeof(float);
 }
@@ -213,10 +225,10 @@ int fwd(const tops_gla_recurrent_args& a, cudaStream_t st) {
   if ((size_t)a.B * a.T * a.H == 0 && a.ht == nullptr) return TOPS_OK;
   if (decode::supported(a)) return decode::fwd(a, st);
   int rows, splits;
-  plan(a.K, rows, splits);
+  fwd_plan(a, rows, splits);
   const size_t need = fwd_workspace(a);
   if (need > 0 && (a.workspace == nullptr || a.workspace_bytes < need))
-    return fail(TOPS_ERR_WORKSPACE, "fused_recurrent: workspace too small for K > 256");
+    return fail(TOPS_ERR_WORKSPACE, "fused_recurrent: workspace smaller than tops_gla_recurrent_fwd_workspace_size()");
   const int vec = (a.V % 4 == 0 && aligned16(a.h0) && aligned16(a.ht)) ? 4 : 1;
   Params p{a.B, a.T, a.H, a.K, a.V, a.N, a.scale, a.reverse, a.cu_seqlens, a.q, a.k, a.v, a.gk, a.gv, a.h0,
            splits > 1 ? static_cast<float*>(a.workspace) : a.o, a.ht};
@@ -504,8 +516,17 @@ __global__ void k_bwd_c(BwdParams bp, int VS, int KS, float* dq, float* dk, floa
   }
 }
 
+// The backward's two passes walk T dependent steps per CTA; splitting K over more CTAs (4 rows
+// per warp) gives the SMs 4x the CTAs to hide each step's latency and quarters the state held
+// per thread.  The K-split partials of dv are summed in pass C.  Measured at H16 K=V=128:
+// B16 T256 4.82 -> 2.43 ms, B64 T64 4.06 -> 1.99 ms (8 rows per warp: 3.55 / 2.65 ms; 2 rows:
+// 2.78 / 2.34 ms).
 static void bwd_plan(const tops_gla_recurrent_args& a, int& rows, int& splits, int& vec, int& vs) {
   plan(a.K, rows, splits);
+  if (rows > 4) {
+    rows = 4;
+    splits = ceil_div(a.K, rows * WARPS);
+  }
   vec = (a.V % 4 == 0) ? 4 : 1;
   vs = ceil_div(a.V, 32 * vec);
 }
