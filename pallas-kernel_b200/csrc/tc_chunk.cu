@@ -1989,8 +1989,9 @@ static int fwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   if (sv.vb != nullptr) v = sv.vb;
   OutMaps om;
   FusedMaps fm{};
-  // fp16 runs the fused kernel only (its epilogue writes fp16; k_out stores bf16 through TMA)
-  const bool fused = o != nullptr && (fused_out() || s.dtype == TOPS_F16);
+  // fp16 and the padded head sizes run the fused kernel only (k_out stores bf16 through TMA, in
+  // 64-column boxes that would lie wholly past V = 64)
+  const bool fused = o != nullptr && (fused_out() || s.dtype == TOPS_F16 || s.K < 128 || s.V < BV);
   if (o != nullptr && !fused)
     okm = okm && map_tok(&om.x, sv.qh, BF, 2, s.B, s.T, s.H, s.K, 64, BT) &&
           map_state(&om.s, sv.h, s.B * NTb * s.H, s.K, s.V, 64) &&
@@ -2122,7 +2123,7 @@ static int bwd_core(const tops_gla_shape& s, const void* q, const void* k, const
   }
   OutMaps om;
   FusedMaps fm{};
-  const bool fused = fused_out() || s.dtype == TOPS_F16;
+  const bool fused = fused_out() || s.dtype == TOPS_F16 || s.K < 128 || s.V < BV;
   if (fused)
     okm = okm && bwd_fused_maps(s, dO, dv, sv, &fm);
   else
