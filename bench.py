@@ -571,6 +571,15 @@ def long_context_bench(args, world, rank, local, dev):
         return max_over_ranks(e0.elapsed_time(e1) / steps, world)
 
     ms = eager_ms = timed(step)
+    # per-launch device times of one eager step (rank 0's), after the timed region
+    from tops import _C
+    _C.timing_enable(True)
+    step()
+    torch.cuda.synchronize()
+    _C.timing_enable(False)
+    kern = {}
+    for nm, t in _C.timing_collect():
+        kern[nm] = round(kern.get(nm, 0.0) + t, 4)
     graph_used = False
     if world > 1:
         # A training loop replays a step this small (a rank's span is 1/N of the sequence) as a
@@ -606,7 +615,7 @@ def long_context_bench(args, world, rank, local, dev):
     return {"metric": "chunk_gla fwd+bwd tokens/s, long context (BASELINE config 4)", "value": B * T / (ms * 1e-3),
             "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
             "timing": "CUDA graph of one step, replayed" if graph_used else "eager launches",
-            "eager_ms_per_step": eager_ms,
+            "eager_ms_per_step": eager_ms, "kernel_ms": kern, "kernel_ms_sum": round(sum(kern.values()), 4),
             "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "T_per_gpu": Tr,
                        "parallelism": "1 GPU (state scans in parallel spans)" if world == 1 else
                        f"sequence spans over {world} GPUs, two-phase span fwd/bwd, one NCCL all-gather "

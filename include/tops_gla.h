@@ -107,7 +107,9 @@ TOPS_API int32_t tops_gla_has_tcgen05(void);
 typedef struct tops_gla_chunk_fwd_args {
   tops_gla_shape s;
   const void* q; const void* k; const void* v;
-  const float* g;              /* [B,T,H,K] log-space gates, NULL = no decay */
+  const float* g;              /* [B,T,H,K] log-space gates, NULL = no decay (zero gates, as the
+                                  reference substitutes; on the tensor-core path they are a zeroed
+                                  region of the workspace, which *_workspace_size then includes) */
   const float* h0;             /* [N,H,K,V] or NULL */
   void* o;                     /* out [B,T,H,V] (dtype); NULL = final state only (ht required) */
   float* ht;                   /* out [N,H,K,V] or NULL (output_final_state=False) */

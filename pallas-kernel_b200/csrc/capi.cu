@@ -160,9 +160,26 @@ static int check_simt_chunk(const tops_gla_shape& s) {
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-// the tensor-core path serves bf16 problems that ask for no CUDA-core-format intermediates
+// the tensor-core path serves bf16 / fp16 problems that ask for no CUDA-core-format intermediates
 static bool use_tc_fwd(const tops_gla_chunk_fwd_args* a) {
-  return a->g != nullptr && a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
+  return a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
+}
+
+// Without gates (g == NULL) the tensor-core kernels read an all-zero gate tensor, as the
+// reference substitutes zeros (tops/ops/gla/chunk.py:1114-1118); it sits at the end of the
+// caller's workspace and is cleared in-stream before use.
+static size_t zero_gate_bytes(const tops_gla_shape& s, const float* g) {
+  return g != nullptr ? 0 : (((size_t)s.B * s.T * s.H * s.K * sizeof(float) + 1023) & ~size_t(1023));
+}
+
+static int zero_gates(const tops_gla_shape& s, void* workspace, size_t offset, const float** g, cudaStream_t st) {
+  if (*g != nullptr) return TOPS_OK;
+  float* z = reinterpret_cast<float*>(static_cast<char*>(workspace) + offset);
+  cudaError_t e = cudaMemsetAsync(z, 0, (size_t)s.B * s.T * s.H * s.K * sizeof(float), st);
+  if (e != cudaSuccess) return cuda_status(e, "chunk: clearing the zero gates");
+  note_launch(1);
+  *g = z;
+  return TOPS_OK;
 }
 
 static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t* ws_need) {
@@ -175,7 +192,9 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
     const bool own = a->saved != nullptr;
     if (own && a->saved_bytes < need_saved)
       return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: saved block smaller than tops_gla_chunk_saved_size()");
-    const size_t need = tc::fwd_workspace(s, own);
+    const size_t base = tc::fwd_workspace(s, own);  // the kernels' own scratch comes first
+    const size_t zb = zero_gate_bytes(s, a->g), zoff = (base + 1023) & ~size_t(1023);
+    const size_t need = zb ? zoff + zb : base;
     if (dry) {
       *ws_need = need;
       return TOPS_OK;
@@ -183,7 +202,9 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
     TOPS_CHECK_ARG(a->q && a->k && a->v && (a->o || a->ht), "chunk_fwd: q, k, v and o (or ht) are required");
     if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need))
       return fail(TOPS_ERR_WORKSPACE, "chunk_fwd: workspace smaller than tops_gla_chunk_fwd_workspace_size()");
-    return tc::fwd(s, a->q, a->k, a->v, a->g, a->h0, a->o, a->ht, own ? a->saved : nullptr, a->workspace, S(stream));
+    const float* g = a->g;
+    if ((rc = zero_gates(s, a->workspace, zoff, &g, S(stream)))) return rc;
+    return tc::fwd(s, a->q, a->k, a->v, g, a->h0, a->o, a->ht, own ? a->saved : nullptr, a->workspace, S(stream));
   }
   if ((rc = check_simt_chunk(s))) return rc;
   if (!dry) {
@@ -217,7 +238,7 @@ static int chunk_fwd_impl(const tops_gla_chunk_fwd_args* a, void* stream, size_t
 // backward
 // ---------------------------------------------------------------------------
 static bool use_tc_bwd(const tops_gla_chunk_bwd_args* a) {
-  return a->g != nullptr && a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
+  return a->g_cumsum == nullptr && a->A == nullptr && a->h == nullptr && tc::eligible(a->s);
 }
 
 static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t* ws_need) {
@@ -231,7 +252,9 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
     const bool have = a->saved != nullptr;
     if (have && a->saved_bytes < tc::saved_bytes(s))
       return fail(TOPS_ERR_WORKSPACE, "chunk_bwd: saved block smaller than tops_gla_chunk_saved_size()");
-    const size_t need = tc::bwd_workspace(s, have);
+    const size_t base = tc::bwd_workspace(s, have);
+    const size_t zb = zero_gate_bytes(s, a->g), zoff = (base + 1023) & ~size_t(1023);
+    const size_t need = zb ? zoff + zb : base;
     if (dry) {
       *ws_need = need;
       return TOPS_OK;
@@ -240,7 +263,9 @@ static int chunk_bwd_impl(const tops_gla_chunk_bwd_args* a, void* stream, size_t
                    "chunk_bwd: q, k, v, do and dq, dk, dv, dg (or dh0 alone) are required");
     if (a->workspace == nullptr || a->workspace_bytes < need)
       return fail(TOPS_ERR_WORKSPACE, "chunk_bwd: workspace smaller than tops_gla_chunk_bwd_workspace_size()");
-    return tc::bwd(s, a->q, a->k, a->v, a->g, a->h0, a->do_, a->dht, a->saved, a->dq, a->dk, a->dv, a->dg, a->dh0,
+    const float* g = a->g;
+    if ((rc = zero_gates(s, a->workspace, zoff, &g, S(stream)))) return rc;
+    return tc::bwd(s, a->q, a->k, a->v, g, a->h0, a->do_, a->dht, a->saved, a->dq, a->dk, a->dv, a->dg, a->dh0,
                    a->workspace, S(stream));
   }
   if ((rc = check_simt_chunk(s))) return rc;

@@ -92,9 +92,8 @@ def _ws(nbytes: int, dev) -> torch.Tensor | None:
 # ---------------------------------------------------------------------------
 
 def saved_size(p: Plan, g) -> int:
-    """Bytes of the tensor-core path's saved block (0 when the problem runs on CUDA cores)."""
-    if g is None:
-        return 0
+    """Bytes of the tensor-core path's saved block (0 when the problem runs on CUDA cores).
+    Ungated problems (g None) take the tensor-core path too: the library substitutes zero gates."""
     s = p.shape()
     return int(_C.lib().tops_gla_chunk_saved_size(s))
 

@@ -118,3 +118,28 @@ def test_tc_varlen_head_sizes(env, K, V, dtype):
                          ("dv", vt.grad, dv_r), ("dg", gt.grad, dg_r), ("dh0", h0t.grad, dh0_r)):
         assert_rel_l2(nm, got, ref, TOL)
         assert_max_rel(nm, got, ref, TOL)
+
+
+def test_tc_ungated(env):
+    """Neither g nor g_gamma on a tensor-core shape: the library substitutes zero gates (as the
+    reference does, chunk.py:1114-1118) and stays on the tensor-core path; fwd + bwd match the
+    oracle with g = None, and equal an explicit all-zero gate bit for bit."""
+    _C, _core, G = env
+    B, T, H, K, V, C = 2, 320, 2, 128, 128, 64
+    q, k, v, _, h0, do, dht = _inputs(21, B, T, H, K, V, torch.bfloat16)
+    plan = _core.make_plan(q, V, C, None, K ** -0.5)
+    assert _core.saved_size(plan, None) > 0, "expected the tensor-core path"
+    qt, kt, vt = (x.clone().requires_grad_() for x in (q, k, v))
+    h0t = h0.clone().requires_grad_()
+    o, ht = G.chunk_gla(qt, kt, vt, initial_state=h0t, output_final_state=True, chunk_size=C)
+    ((o.float() * do.float()).sum() + (ht * dht).sum()).backward()
+    z = torch.zeros(B, T, H, K, device="cuda")
+    o0, ht0 = G.chunk_gla(q, k, v, z, initial_state=h0, output_final_state=True, chunk_size=C)
+    assert torch.equal(o.detach(), o0) and torch.equal(ht.detach(), ht0), "ungated differs from g = 0"
+    qn, kn, vn, h0n, don, dhtn = (x.float().cpu().numpy() for x in (q, k, v, h0, do, dht))
+    o_r, ht_r = O.chunk_gla(qn, kn, vn, None, initial_state=h0n, output_final_state=True, chunk_size=C)
+    dq_r, dk_r, dv_r, _, dh0_r = O.chunk_gla_bwd(qn, kn, vn, None, None, K ** -0.5, h0n, None, None, don, dhtn,
+                                                 None, C)
+    for nm, got, ref in (("o", o, o_r), ("ht", ht, ht_r), ("dq", qt.grad, dq_r), ("dk", kt.grad, dk_r),
+                         ("dv", vt.grad, dv_r), ("dh0", h0t.grad, dh0_r)):
+        assert_rel_l2(nm, got, ref, TOL)
