@@ -547,16 +547,15 @@ def long_context_bench(args, world, rank, local, dev):
             return _core.chunk_bwd(plan, q, k, v, g, None, do, None, block=sv.get("block"))
     else:
         from tops import distributed as TD
-        ex = TD.NcclStateExchange()
         for x in (q, k, v, g):
             x.requires_grad_()
 
-        def step():
-            o, _ = TD.chunk_gla_seq_parallel(q, k, v, g, chunk_size=C, exchange=ex)
-            return torch.autograd.grad(o, (q, k, v, g), do)
+        def step_with(ex):
+            def step():
+                o, _ = TD.chunk_gla_seq_parallel(q, k, v, g, chunk_size=C, exchange=ex)
+                return torch.autograd.grad(o, (q, k, v, g), do)
+            return step
 
-    for _ in range(3):
-        step()
     steps = max(3, min(args.steps, 5))
 
     def timed(run):
@@ -570,56 +569,83 @@ def long_context_bench(args, world, rank, local, dev):
         barrier(world)
         return max_over_ranks(e0.elapsed_time(e1) / steps, world)
 
-    ms = eager_ms = timed(step)
-    # per-launch device times of one eager step (rank 0's), after the timed region
-    from tops import _C
-    _C.timing_enable(True)
-    step()
-    torch.cuda.synchronize()
-    _C.timing_enable(False)
-    kern = {}
-    for nm, t in _C.timing_collect():
-        kern[nm] = round(kern.get(nm, 0.0) + t, 4)
-    graph_used = False
-    if world > 1:
-        # A training loop replays a step this small (a rank's span is 1/N of the sequence) as a
-        # CUDA graph, so the host's launch and autograd work stops adding to the step.  The graph
-        # holds the same kernels and NCCL all-gathers; every rank replays only if every rank
-        # captured (the collectives must pair up), and the graph is released before the
-        # communicator and the process group.
-        import torch.distributed as dist
-        graph, ok = None, 1
-        try:
-            side = torch.cuda.Stream(dev)
-            side.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(side):
-                for _ in range(2):
-                    step()
-            torch.cuda.current_stream(dev).wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                step()
-            graph.replay()
-            torch.cuda.synchronize(dev)
-        except Exception:
-            graph, ok = None, 0
-        flag = torch.tensor([ok], device=dev, dtype=torch.int32)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        if int(flag.item()) == 1:
-            ms = timed(graph.replay)
-            graph_used = True
-        del graph
+    def measure(step):
+        """-> (ms per step, eager ms per step, per-launch ms of one eager step, graph used)."""
+        for _ in range(3):
+            step()
+        ms = eager_ms = timed(step)
+        # per-launch device times of one eager step (rank 0's), after the timed region
+        from tops import _C
+        _C.timing_enable(True)
+        step()
         torch.cuda.synchronize()
+        _C.timing_enable(False)
+        kern = {}
+        for nm, t in _C.timing_collect():
+            kern[nm] = round(kern.get(nm, 0.0) + t, 4)
+        graph_used = False
+        if world > 1:
+            # A training loop replays a step this small (a rank's span is 1/N of the sequence)
+            # as a CUDA graph, so the host's launch and autograd work stops adding to the step.
+            # The graph holds the same kernels and exchanges; every rank replays only if every
+            # rank captured (the exchanges must pair up), and the graph is released before the
+            # exchange and the process group.
+            import torch.distributed as dist
+            graph, ok = None, 1
+            try:
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    for _ in range(2):
+                        step()
+                torch.cuda.current_stream(dev).wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    step()
+                graph.replay()
+                torch.cuda.synchronize(dev)
+            except Exception:
+                graph, ok = None, 0
+            flag = torch.tensor([ok], device=dev, dtype=torch.int32)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()) == 1:
+                ms = timed(graph.replay)
+                graph_used = True
+            del graph
+            torch.cuda.synchronize()
+        return ms, eager_ms, kern, graph_used
+
+    route, nccl_route = "none (1 GPU)", None
+    if world == 1:
+        ms, eager_ms, kern, graph_used = measure(step)
+    else:
+        # the product route: the state exchange through peer memory (two kernels, NVLink
+        # stores); the C ABI's NCCL all-gather route is timed the same way beside it
+        try:
+            ex = TD.P2PStateExchange()
+            route = "peer memory (tops_gla_p2p_exchange)"
+        except (ValueError, RuntimeError):
+            ex = TD.NcclStateExchange()
+            route = "NCCL all-gather (tops_gla_state_exchange)"
+        ms, eager_ms, kern, graph_used = measure(step_with(ex))
         ex.close()
+        if isinstance(ex, TD.P2PStateExchange):
+            ex2 = TD.NcclStateExchange()
+            n_ms, n_eager, n_kern, n_graph = measure(step_with(ex2))
+            ex2.close()
+            nccl_route = {"ms_per_step": n_ms, "eager_ms_per_step": n_eager,
+                          "timing": "CUDA graph of one step, replayed" if n_graph else "eager launches",
+                          "exchange_kernel_ms": {k_: v_ for k_, v_ in n_kern.items() if k_.startswith("exchange")}}
     del q, k, v, g, do
     return {"metric": "chunk_gla fwd+bwd tokens/s, long context (BASELINE config 4)", "value": B * T / (ms * 1e-3),
             "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
             "timing": "CUDA graph of one step, replayed" if graph_used else "eager launches",
             "eager_ms_per_step": eager_ms, "kernel_ms": kern, "kernel_ms_sum": round(sum(kern.values()), 4),
+            "exchange": route, "nccl_route": nccl_route,
             "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "T_per_gpu": Tr,
                        "parallelism": "1 GPU (state scans in parallel spans)" if world == 1 else
-                       f"sequence spans over {world} GPUs, two-phase span fwd/bwd, one NCCL all-gather "
-                       "of (state, decay) per direction"}}
+                       f"sequence spans over {world} GPUs, two-phase span fwd/bwd, one exchange of "
+                       "(state, decay) per direction"}}
 
 
 def strong_cfg3_bench(args, world, rank, dev):

@@ -92,7 +92,8 @@ TOPS_API void tops_gla_timing_enable(int32_t on);
 TOPS_API int32_t tops_gla_timing_collect(char* names, int32_t name_stride, float* ms, int32_t max_entries);
 TOPS_API int32_t tops_gla_abi_version(void);
 /* First error code recorded by a device-side bounded wait since the last call
- * (0 = none, 1 = an mbarrier wait timed out); reading clears it.  Synchronizes. */
+ * (0 = none, 1 = an mbarrier wait timed out, 3 = a peer-memory exchange gave up waiting for
+ * a rank); reading clears it.  Synchronizes. */
 TOPS_API int32_t tops_gla_device_error(void);
 /* Check of the failure path: launches one thread that waits on an mbarrier nothing will
  * complete, so its bounded wait runs out (about 2 s) and records code 1 for
@@ -348,6 +349,46 @@ TOPS_API int tops_gla_nccl_comm_destroy(void* comm);
 TOPS_API int tops_gla_nccl_comm_abort(void* comm);
 TOPS_API int tops_gla_nccl_comm_check(void* comm);
 TOPS_API int tops_gla_state_exchange_wait(void* comm, void* stream, int32_t timeout_ms);
+
+/* The same exchange through peer memory instead of NCCL: one process per GPU, every rank's
+ * receive region mapped into every process (CUDA IPC; NVLink / NVSwitch peer access).
+ * p2p_exchange runs two kernels on `stream`: this rank's packed (state | decay) is stored
+ * straight into its slot of every rank's region and, once all of it is written, an epoch flag
+ * into every region; then the prefix (forward: out = this rank's incoming state, total = the
+ * whole sequence's final state) or suffix (backward: out = this rank's final-state gradient)
+ * of tops_gla_state_exchange, computed from this rank's own region after every rank's flag
+ * for the epoch has arrived.  The results are bit-identical to tops_gla_state_exchange.  The
+ * wait is bounded: after timeout_ms it records device error 3 and leaves `out` unwritten.
+ * The epoch lives in the region (device memory), so the two kernels can be captured in a CUDA
+ * graph and replayed.  Every rank must run the same sequence of exchanges on one region.
+ * regions: device array [world] of every rank's region as mapped in this process (this
+ * rank's own included); own_region: this rank's.  At most 64 ranks.
+ * region_size: bytes of one region (a 4 KB control block and two slots per rank);
+ * p2p_alloc / p2p_free: a zeroed region from cudaMalloc (IPC needs a whole allocation);
+ * ipc_handle / ipc_open / ipc_close: cudaIpcGetMemHandle / cudaIpcOpenMemHandle (peer
+ * access enabled) / cudaIpcCloseMemHandle, handle = TOPS_GLA_IPC_HANDLE_BYTES bytes.
+ * No reference counterpart (the reference has no multi-device code). */
+#define TOPS_GLA_IPC_HANDLE_BYTES 64
+typedef struct tops_gla_p2p_args {
+  int32_t rank, world;
+  int32_t N, H, K, V;
+  int32_t backward;
+  const float* local_state;
+  const float* decay;
+  const float* boundary;
+  float* out;
+  float* total;
+  void* const* regions;
+  void* own_region;
+  int32_t timeout_ms;
+} tops_gla_p2p_args;
+TOPS_API size_t tops_gla_p2p_region_size(const tops_gla_p2p_args* a);
+TOPS_API int tops_gla_p2p_alloc(size_t bytes, void** region);
+TOPS_API int tops_gla_p2p_free(void* region);
+TOPS_API int tops_gla_ipc_handle(const void* region, void* handle);
+TOPS_API int tops_gla_ipc_open(const void* handle, void** region);
+TOPS_API int tops_gla_ipc_close(void* region);
+TOPS_API int tops_gla_p2p_exchange(const tops_gla_p2p_args* a, void* stream);
 
 /* ---- GLA layer pieces around the chunked op ------------ */
 

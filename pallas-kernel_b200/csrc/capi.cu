@@ -116,6 +116,10 @@ namespace decode {
 int read_device_error();
 }  // namespace decode
 
+namespace exchange {
+int read_device_error();
+}  // namespace exchange
+
 namespace tc {
 bool eligible(const tops_gla_shape& s);
 size_t saved_bytes(const tops_gla_shape& s);
@@ -356,9 +360,10 @@ const char* tops_gla_last_error(void) { return g_last_error.c_str(); }
 uint64_t tops_gla_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int32_t tops_gla_device_error(void) {
-  int32_t e = decode::read_device_error();
+  const int32_t e = decode::read_device_error();
   const int32_t e2 = tc::read_device_error();
-  return e != 0 ? e : e2;
+  const int32_t e3 = exchange::read_device_error();  // every word is read (and cleared)
+  return e != 0 ? e : e2 != 0 ? e2 : e3;
 }
 
 int tops_gla_selftest_wait_timeout(void* stream) {

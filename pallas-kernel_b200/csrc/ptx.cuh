@@ -17,6 +17,7 @@ enum : int {
   DEVERR_NONE = 0,
   DEVERR_MBAR_TIMEOUT = 1,   // an mbarrier wait exceeded its limit
   DEVERR_BAD_LAUNCH = 2,     // kernel launched with an unsupported configuration
+  DEVERR_PEER_TIMEOUT = 3,   // a peer-memory exchange waited longer than its limit for a rank
 };
 // One error word per translation unit (no relocatable device code); each .cu that
 // launches waiting kernels exposes it through TOPS_DEVICE_ERROR_READER.

@@ -75,6 +75,14 @@ class ExchangeArgs(C.Structure):
                 ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
 
 
+class P2PArgs(C.Structure):
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("N", C.c_int32), ("H", C.c_int32), ("K", C.c_int32),
+                ("V", C.c_int32), ("backward", C.c_int32), ("local_state", C.c_void_p), ("decay", C.c_void_p),
+                ("boundary", C.c_void_p), ("out", C.c_void_p), ("total", C.c_void_p), ("regions", C.c_void_p),
+                ("own_region", C.c_void_p), ("timeout_ms", C.c_int32)]
+
+
+IPC_HANDLE_BYTES = 64
 VP, I32, F32C = C.c_void_p, C.c_int32, C.c_float
 SIGNATURES = {
     "tops_gla_last_error": (C.c_char_p, []),
@@ -128,6 +136,13 @@ SIGNATURES = {
     "tops_gla_nccl_comm_abort": (C.c_int, [VP]),
     "tops_gla_nccl_comm_check": (C.c_int, [VP]),
     "tops_gla_state_exchange_wait": (C.c_int, [VP, VP, I32]),
+    "tops_gla_p2p_region_size": (C.c_size_t, [C.POINTER(P2PArgs)]),
+    "tops_gla_p2p_alloc": (C.c_int, [C.c_size_t, C.POINTER(VP)]),
+    "tops_gla_p2p_free": (C.c_int, [VP]),
+    "tops_gla_ipc_handle": (C.c_int, [VP, VP]),
+    "tops_gla_ipc_open": (C.c_int, [VP, C.POINTER(VP)]),
+    "tops_gla_ipc_close": (C.c_int, [VP]),
+    "tops_gla_p2p_exchange": (C.c_int, [C.POINTER(P2PArgs), VP]),
     "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),

@@ -34,7 +34,7 @@ import torch.distributed as dist
 
 __all__ = ["shard", "prefix_states", "suffix_grads", "all_gather_stack", "seq_parallel_forward",
            "seq_parallel_backward", "seq_parallel_forward_phased", "seq_parallel_backward_phased",
-           "chunk_gla_seq_parallel", "NcclStateExchange", "PeerWatchdog", "PeerLostError"]
+           "chunk_gla_seq_parallel", "NcclStateExchange", "P2PStateExchange", "PeerWatchdog", "PeerLostError"]
 
 
 class PeerLostError(RuntimeError):
@@ -193,6 +193,143 @@ class NcclStateExchange:
         if self.comm:
             self._C.call("tops_gla_nccl_comm_destroy", self.comm)
             self.comm = ctypes.c_void_p()
+        if self.watchdog is not None:
+            self.watchdog.close()
+            self.watchdog = None
+
+
+class P2PStateExchange:
+    """The state exchange through peer memory (``tops_gla_p2p_exchange``): every rank's
+    packed (state, decay) goes straight into its slot of every rank's receive region over
+    NVLink, an epoch flag follows, and each rank folds the prefix / suffix from its own region
+    once every rank's flag has arrived -- two kernels, no NCCL launch, bit-identical to
+    :class:`NcclStateExchange`.  One process per GPU of one host; every rank of the group must
+    construct it and run the same exchanges in the same order (as with any collective).
+
+    A region per (N, H, K, V) is allocated on first use (collectively: IPC handles are
+    exchanged through the group, then every rank maps every region), so the first exchange of
+    a shape must not be inside a CUDA-graph capture; later ones can be captured and replayed
+    (the epoch lives in device memory).  Failure handling: the same host-side
+    :class:`PeerWatchdog` check before every exchange as NcclStateExchange, and the device-side
+    wait for a peer's flag gives up after ``timeout_s`` (device error 3, output not written)."""
+
+    _made = 0
+
+    def __init__(self, group=None, liveness_timeout: float | None = 30.0, timeout_s: float = 10.0):
+        import socket
+
+        from . import _C
+        self._C = _C
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.timeout_ms = max(1, int(timeout_s * 1000))
+        where = [None] * self.world
+        dist.all_gather_object(where, (socket.gethostname(), str(torch.cuda.get_device_properties(self.device).uuid)),
+                               group=group)
+        if len({h for h, _ in where}) != 1 or len({u for _, u in where}) != self.world:
+            raise ValueError("P2PStateExchange needs one process per GPU on one host (use NcclStateExchange)")
+        self.regions = {}  # (N, H, K, V) -> (own region, [mapped peer regions], device table of all)
+        self.watchdog = None
+        P2PStateExchange._made += 1
+        if liveness_timeout is not None and group is None:
+            self.watchdog = PeerWatchdog(timeout=liveness_timeout, prefix=f"tops_gla/p2p{P2PStateExchange._made}")
+
+    def _args(self, shape, backward=0):
+        N, H, K, V = shape
+        return self._C.P2PArgs(self.rank, self.world, N, H, K, V, int(backward), None, None, None, None, None, None,
+                               None, self.timeout_ms)
+
+    def _region(self, shape):
+        reg = self.regions.get(shape)
+        if reg is not None:
+            return reg
+        C, L = self._C, self._C.lib()
+        nbytes = int(L.tops_gla_p2p_region_size(ctypes.byref(self._args(shape))))
+        own = ctypes.c_void_p()
+        C.call("tops_gla_p2p_alloc", nbytes, ctypes.byref(own))
+        handle = (ctypes.c_char * C.IPC_HANDLE_BYTES)()
+        C.call("tops_gla_ipc_handle", own, ctypes.addressof(handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        mapped, ptrs = [], []
+        for j, hb in enumerate(handles):
+            if j == self.rank:
+                ptrs.append(own.value)
+                continue
+            buf = (ctypes.c_char * C.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+            p = ctypes.c_void_p()
+            C.call("tops_gla_ipc_open", ctypes.addressof(buf), ctypes.byref(p))
+            mapped.append(p)
+            ptrs.append(p.value)
+        table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        dist.barrier(group=self.group)  # every region is mapped everywhere before the first push
+        reg = self.regions[shape] = (own, mapped, table)
+        return reg
+
+    def check_peers(self) -> None:
+        """Raise PeerLostError if a peer is gone (before any exchange kernel is launched)."""
+        if self.watchdog is not None:
+            self.watchdog.check()
+
+    def abort(self) -> None:
+        """Stop watching the peers (there is no communicator; the kernels' own waits are
+        bounded)."""
+        if self.watchdog is not None:
+            self.watchdog.close()
+            self.watchdog = None
+
+    def wait(self, timeout_s: float, stream=None) -> None:
+        """Wait on the host, at most ``timeout_s``, for the exchanges enqueued so far; raise
+        TopsError at the deadline or if a device-side wait for a peer gave up."""
+        ev = torch.cuda.Event()
+        ev.record(stream if stream is not None else torch.cuda.current_stream(self.device))
+        deadline = time.monotonic() + timeout_s
+        while not ev.query():
+            if time.monotonic() > deadline:
+                raise self._C.TopsError("P2PStateExchange.wait", -5, f"exchange not done after {timeout_s} s")
+            time.sleep(0.0002)
+        code = int(self._C.lib().tops_gla_device_error())
+        if code:
+            raise self._C.TopsError("P2PStateExchange.wait", -5, f"device wait for a peer gave up (error {code})")
+
+    def _run(self, backward: bool, local: torch.Tensor, decay: torch.Tensor, boundary, want_total: bool):
+        C = self._C
+        self.check_peers()
+        local = local.float().contiguous()
+        decay = decay.float().contiguous()
+        boundary = None if boundary is None else boundary.float().contiguous()
+        shape = tuple(local.shape)
+        own, _, table = self._region(shape)
+        out = torch.empty_like(local)
+        total = torch.empty_like(local) if want_total else None
+        a = self._args(shape, backward)
+        a.local_state, a.decay, a.boundary = C.ptr(local), C.ptr(decay), C.ptr(boundary)
+        a.out, a.total, a.regions, a.own_region = C.ptr(out), C.ptr(total), C.ptr(table), own.value
+        C.call("tops_gla_p2p_exchange", a, C.stream_of(local))
+        return out, total
+
+    def forward(self, S, D, h0=None):
+        """-> (this rank's incoming state, the whole sequence's final state)."""
+        return self._run(False, S, D, h0, True)
+
+    def backward(self, L, D, dht=None):
+        """-> the final-state gradient this rank's backward must use."""
+        return self._run(True, L, D, dht, False)[0]
+
+    def close(self):
+        """Unmap and free the regions (collective: no rank frees its region while another may
+        still write into it)."""
+        if self.regions:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            for own, mapped, _ in self.regions.values():
+                for p in mapped:
+                    self._C.call("tops_gla_ipc_close", p)
+            dist.barrier(group=self.group)
+            for own, _, _ in self.regions.values():
+                self._C.call("tops_gla_p2p_free", own)
+            self.regions = {}
         if self.watchdog is not None:
             self.watchdog.close()
             self.watchdog = None

@@ -48,7 +48,7 @@ def test_struct_layouts_match_ctypes(lib, tmp_path):
     structs = {"tops_gla_shape": lib.Shape, "tops_gla_chunk_fwd_args": lib.ChunkFwdArgs,
                "tops_gla_xla_desc": lib.XlaDesc, "tops_gla_exchange_args": lib.ExchangeArgs,
                "tops_gla_chunk_bwd_args": lib.ChunkBwdArgs, "tops_gla_recurrent_args": lib.RecArgs,
-               "tops_gla_recurrent_bwd_args": lib.RecBwdArgs}
+               "tops_gla_recurrent_bwd_args": lib.RecBwdArgs, "tops_gla_p2p_args": lib.P2PArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
@@ -162,3 +162,26 @@ def test_nccl_failure_entry_points_validate_without_a_device(lib):
     assert L.tops_gla_state_exchange_wait(None, None, 100) == -1
     assert L.tops_gla_state_exchange_wait(1, None, 0) == -1
     assert b"positive timeout" in L.tops_gla_last_error()
+
+
+def test_p2p_exchange_entry_points_validate_without_a_device(lib):
+    """The peer-memory exchange sizes its region from the shape alone and rejects bad ranks,
+    missing buffers and a non-positive timeout before launching anything; freeing or closing a
+    NULL region is a no-op."""
+    import ctypes
+    L = lib.lib()
+    a = lib.P2PArgs(0, 2, 1, 16, 128, 128, 0, None, None, None, None, None, None, None, 1000)
+    per = 16 * 128 * 128 + 16 * 128
+    assert L.tops_gla_p2p_region_size(ctypes.byref(a)) == 4096 + 2 * 2 * per * 4
+    assert L.tops_gla_p2p_exchange(ctypes.byref(a), None) == -1  # no buffers
+    a.local_state = a.decay = a.out = a.regions = a.own_region = 16
+    a.rank = 2
+    assert L.tops_gla_p2p_exchange(ctypes.byref(a), None) == -1
+    assert b"rank / world" in L.tops_gla_last_error()
+    a.rank, a.world = 0, 65
+    assert L.tops_gla_p2p_region_size(ctypes.byref(a)) == 0
+    a.world, a.timeout_ms = 2, 0
+    assert L.tops_gla_p2p_exchange(ctypes.byref(a), None) == -1
+    assert b"timeout_ms" in L.tops_gla_last_error()
+    assert L.tops_gla_p2p_free(None) == 0 and L.tops_gla_ipc_close(None) == 0
+    assert L.tops_gla_ipc_handle(None, None) == -1

@@ -57,22 +57,39 @@ def _worker(rank, world, port, out, use_exchange=False):
     q, k, v, g, h0, do, dht = _inputs(dev)
     T = q.shape[1]
     sl = slice(rank * T // world, (rank + 1) * T // world)
-    qs, ks, vs, gs = (x[:, sl].contiguous().requires_grad_() for x in (q, k, v, g))
-    h0r = h0.clone().requires_grad_()
-    ex = TD.NcclStateExchange() if use_exchange else None
-    o, ht = TD.chunk_gla_seq_parallel(qs, ks, vs, gs, initial_state=h0r, chunk_size=64, exchange=ex)
-    loss = (o.float() * do[:, sl].float()).sum() + (ht * dht).sum()  # ht and dht are replicated
-    loss.backward()
-    if ex is not None:  # the bounded host wait returns once the exchanges are done; no peer is lost
-        ex.wait(30.0)
-        ex.check_peers()
-    res = dict(o=o.detach().cpu(), ht=ht.detach().cpu(), dq=qs.grad.cpu(), dk=ks.grad.cpu(), dv=vs.grad.cpu(),
-               dg=gs.grad.cpu())
-    if rank == 0:
-        res["dh0"] = h0r.grad.cpu()
+
+    def step(ex):
+        qs, ks, vs, gs = (x[:, sl].contiguous().requires_grad_() for x in (q, k, v, g))
+        h0r = h0.clone().requires_grad_()
+        o, ht = TD.chunk_gla_seq_parallel(qs, ks, vs, gs, initial_state=h0r, chunk_size=64, exchange=ex)
+        loss = (o.float() * do[:, sl].float()).sum() + (ht * dht).sum()  # ht and dht are replicated
+        loss.backward()
+        if ex is not None:  # the bounded host wait returns once the exchanges are done; no peer is lost
+            ex.wait(30.0)
+            ex.check_peers()
+        res = dict(o=o.detach().cpu(), ht=ht.detach().cpu(), dq=qs.grad.cpu(), dk=ks.grad.cpu(), dv=vs.grad.cpu(),
+                   dg=gs.grad.cpu())
+        if rank == 0:
+            res["dh0"] = h0r.grad.cpu()
+        return res
+
+    exs = []
+    if use_exchange == "nccl":
+        exs.append(TD.NcclStateExchange())
+    elif use_exchange == "p2p":
+        exs.append(TD.P2PStateExchange())
+    res = step(exs[0] if exs else None)
+    if use_exchange == "p2p":
+        # the peer route equals the NCCL route bit for bit (the same combine arithmetic); a
+        # step's forward and backward exchanges use the two slot parities, and the second peer
+        # step reuses both slots
+        exs.append(TD.NcclStateExchange())
+        ref = step(exs[1])
+        again = step(exs[0])
+        res["same_as_nccl"] = all(torch.equal(res[nm], ref[nm]) and torch.equal(again[nm], ref[nm]) for nm in ref)
     out[rank] = res
-    if ex is not None:
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    for ex in exs:
         ex.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -80,7 +97,8 @@ def _worker(rank, world, port, out, use_exchange=False):
 
 @pytest.mark.timeout(600)
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("use_exchange", [False, True], ids=["torch-all-gather", "c-abi-nccl-exchange"])
+@pytest.mark.parametrize("use_exchange", [None, "nccl", "p2p"],
+                         ids=["torch-all-gather", "c-abi-nccl-exchange", "c-abi-peer-memory-exchange"])
 def test_seq_parallel_two_gpus_matches_one_gpu(gla, use_exchange):
     world = 2
     ctx = mp.get_context("spawn")
@@ -110,3 +128,6 @@ def test_seq_parallel_two_gpus_matches_one_gpu(gla, use_exchange):
     for nm, ref in (("dq", qs.grad), ("dk", ks.grad), ("dv", vs.grad), ("dg", gs.grad)):
         assert rel(cat(nm), ref.cpu()) < 2e-2, nm
     assert rel(out[0]["dh0"], h0r.grad.cpu()) < 2e-2
+    if use_exchange == "p2p":
+        for r in range(world):
+            assert out[r]["same_as_nccl"], f"rank {r}: the peer-memory exchange differs from the NCCL one"
