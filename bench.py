@@ -621,10 +621,14 @@ def long_context_bench(args, world, rank, local, dev):
     else:
         # the product route: the state exchange through peer memory (two kernels, NVLink
         # stores); the C ABI's NCCL all-gather route is timed the same way beside it
-        try:
+        ex = None
+        try:  # construction and region setup are collective and fail on every rank together
             ex = TD.P2PStateExchange()
+            ex.prepare((B, H, K, V))
             route = "peer memory (tops_gla_p2p_exchange)"
         except (ValueError, RuntimeError):
+            if ex is not None:
+                ex.close()
             ex = TD.NcclStateExchange()
             route = "NCCL all-gather (tops_gla_state_exchange)"
         ms, eager_ms, kern, graph_used = measure(step_with(ex))

@@ -245,27 +245,50 @@ class P2PStateExchange:
         if reg is not None:
             return reg
         C, L = self._C, self._C.lib()
-        nbytes = int(L.tops_gla_p2p_region_size(ctypes.byref(self._args(shape))))
-        own = ctypes.c_void_p()
-        C.call("tops_gla_p2p_alloc", nbytes, ctypes.byref(own))
-        handle = (ctypes.c_char * C.IPC_HANDLE_BYTES)()
-        C.call("tops_gla_ipc_handle", own, ctypes.addressof(handle))
+        own, mapped, handle, err = ctypes.c_void_p(), [], None, None
+        try:
+            nbytes = int(L.tops_gla_p2p_region_size(ctypes.byref(self._args(shape))))
+            C.call("tops_gla_p2p_alloc", nbytes, ctypes.byref(own))
+            hbuf = (ctypes.c_char * C.IPC_HANDLE_BYTES)()
+            C.call("tops_gla_ipc_handle", own, ctypes.addressof(hbuf))
+            handle = bytes(hbuf)
+        except Exception as e:  # noqa: BLE001 -- every rank must learn of it before going on
+            err = f"{type(e).__name__}: {e}"
         handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=self.group)
-        mapped, ptrs = [], []
-        for j, hb in enumerate(handles):
-            if j == self.rank:
-                ptrs.append(own.value)
-                continue
-            buf = (ctypes.c_char * C.IPC_HANDLE_BYTES).from_buffer_copy(hb)
-            p = ctypes.c_void_p()
-            C.call("tops_gla_ipc_open", ctypes.addressof(buf), ctypes.byref(p))
-            mapped.append(p)
-            ptrs.append(p.value)
+        dist.all_gather_object(handles, (handle, err), group=self.group)
+        ptrs = []
+        if all(h is not None for h, _ in handles):
+            try:
+                for j, (hb, _) in enumerate(handles):
+                    if j == self.rank:
+                        ptrs.append(own.value)
+                        continue
+                    buf = (ctypes.c_char * C.IPC_HANDLE_BYTES).from_buffer_copy(hb)
+                    pj = ctypes.c_void_p()
+                    C.call("tops_gla_ipc_open", ctypes.addressof(buf), ctypes.byref(pj))
+                    mapped.append(pj)
+                    ptrs.append(pj.value)
+            except Exception as e:  # noqa: BLE001
+                err = f"{type(e).__name__}: {e}"
+        outcome = [None] * self.world
+        dist.all_gather_object(outcome, err, group=self.group)
+        failed = [(j, e) for j, e in enumerate(outcome) if e is not None]
+        if failed:  # every rank unwinds and raises together, so their collectives stay paired
+            for pj in mapped:
+                C.lib().tops_gla_ipc_close(pj)
+            dist.barrier(group=self.group)
+            if own.value:
+                C.lib().tops_gla_p2p_free(own)
+            raise RuntimeError(f"peer-memory regions could not be set up: rank {failed[0][0]}: {failed[0][1]}")
         table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         dist.barrier(group=self.group)  # every region is mapped everywhere before the first push
         reg = self.regions[shape] = (own, mapped, table)
         return reg
+
+    def prepare(self, shape) -> None:
+        """Set up the regions for states of ``shape`` = (N, H, K, V) now (collective).  Raises
+        RuntimeError on every rank if any rank could not allocate or map them."""
+        self._region(tuple(int(x) for x in shape))
 
     def check_peers(self) -> None:
         """Raise PeerLostError if a peer is gone (before any exchange kernel is launched)."""
