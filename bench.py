@@ -615,7 +615,7 @@ def long_context_bench(args, world, rank, local, dev):
             torch.cuda.synchronize()
         return ms, eager_ms, kern, graph_used
 
-    route, nccl_route = "none (1 GPU)", None
+    route, nccl_route, p2p_unfused_route = "none (1 GPU)", None, None
     if world == 1:
         ms, eager_ms, kern, graph_used = measure(step)
     else:
@@ -634,18 +634,23 @@ def long_context_bench(args, world, rank, local, dev):
         ms, eager_ms, kern, graph_used = measure(step_with(ex))
         ex.close()
         if isinstance(ex, TD.P2PStateExchange):
-            ex2 = TD.NcclStateExchange()
-            n_ms, n_eager, n_kern, n_graph = measure(step_with(ex2))
-            ex2.close()
-            nccl_route = {"ms_per_step": n_ms, "eager_ms_per_step": n_eager,
-                          "timing": "CUDA graph of one step, replayed" if n_graph else "eager launches",
-                          "exchange_kernel_ms": {k_: v_ for k_, v_ in n_kern.items() if k_.startswith("exchange")}}
+            route = "peer memory, pushed by the span kernel that computes the state (tops_gla_chunk_*_span_begin_p2p)"
+
+            def other(make):
+                e2 = make()
+                o_ms, o_eager, o_kern, o_graph = measure(step_with(e2))
+                e2.close()
+                return {"ms_per_step": o_ms, "eager_ms_per_step": o_eager,
+                        "timing": "CUDA graph of one step, replayed" if o_graph else "eager launches",
+                        "exchange_kernel_ms": {k_: v_ for k_, v_ in o_kern.items() if k_.startswith("exchange")}}
+            p2p_unfused_route = other(lambda: TD.P2PStateExchange(fused=False))
+            nccl_route = other(TD.NcclStateExchange)
     del q, k, v, g, do
     return {"metric": "chunk_gla fwd+bwd tokens/s, long context (BASELINE config 4)", "value": B * T / (ms * 1e-3),
             "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "scaling": "strong",
             "timing": "CUDA graph of one step, replayed" if graph_used else "eager launches",
             "eager_ms_per_step": eager_ms, "kernel_ms": kern, "kernel_ms_sum": round(sum(kern.values()), 4),
-            "exchange": route, "nccl_route": nccl_route,
+            "exchange": route, "p2p_unfused_route": p2p_unfused_route, "nccl_route": nccl_route,
             "config": {"B": B, "T": T, "H": H, "K": K, "V": V, "chunk_size": C, "T_per_gpu": Tr,
                        "parallelism": "1 GPU (state scans in parallel spans)" if world == 1 else
                        f"sequence spans over {world} GPUs, two-phase span fwd/bwd, one exchange of "

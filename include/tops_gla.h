@@ -389,6 +389,20 @@ TOPS_API int tops_gla_ipc_handle(const void* region, void* handle);
 TOPS_API int tops_gla_ipc_open(const void* handle, void** region);
 TOPS_API int tops_gla_ipc_close(void* region);
 TOPS_API int tops_gla_p2p_exchange(const tops_gla_p2p_args* a, void* stream);
+/* The two halves of p2p_exchange apart, for a producer that pushes its own state:
+ * p2p_combine is the wait + prefix / suffix kernel alone (the push must have been made by
+ * one of the span_begin_p2p calls below, or by p2p_exchange's own push, for this epoch).
+ * chunk_{fwd,bwd}_span_begin_p2p are tops_gla_chunk_{fwd,bwd}_span_begin with the state
+ * exchange's push fused into the kernel that computes the span's own state: the rank's
+ * (S | D) -- backward (L | D), D = the forward's span decay passed in -- goes straight from
+ * that kernel into every rank's region, followed by the epoch flags; no local copy of S or
+ * L is written.  The forward still writes `decay` (kept for the backward).  x->N, H, K, V
+ * must be the problem's B, H, K, V; x's rank, world, regions and own_region are used. */
+TOPS_API int tops_gla_p2p_combine(const tops_gla_p2p_args* a, void* stream);
+TOPS_API int tops_gla_chunk_fwd_span_begin_p2p(const tops_gla_chunk_fwd_args* a, float* decay,
+                                               const tops_gla_p2p_args* x, void* stream);
+TOPS_API int tops_gla_chunk_bwd_span_begin_p2p(const tops_gla_chunk_bwd_args* a, const float* decay,
+                                               const tops_gla_p2p_args* x, void* stream);
 
 /* ---- GLA layer pieces around the chunked op ------------ */
 

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "p2p.cuh"
 
 namespace tops {
 
@@ -131,11 +132,11 @@ int selftest_wait_timeout(cudaStream_t st);
 size_t span_saved_bytes(const tops_gla_shape& s);
 size_t bwd_span_workspace(const tops_gla_shape& s);
 int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, void* saved,
-                   float* local_state, float* decay, cudaStream_t st);
+                   float* local_state, float* decay, cudaStream_t st, const p2p::PeerPush* push = nullptr);
 int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
                     const float* h_in, void* o, float* ht, void* saved, cudaStream_t st);
 int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, void* workspace, float* local_dh0,
-                   cudaStream_t st);
+                   cudaStream_t st, const p2p::PeerPush* push = nullptr);
 int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
                     const void* dO, const float* dht_in, const void* saved, void* dq, void* dk, void* dv, float* dg,
                     float* dh0, void* workspace, cudaStream_t st);
@@ -468,6 +469,27 @@ int tops_gla_chunk_fwd_span_begin(const tops_gla_chunk_fwd_args* a, float* local
   return tc::fwd_span_begin(a->s, a->q, a->k, a->v, a->g, a->saved, local_state, decay, S(stream));
 }
 
+// the peer-memory arguments of a fused span begin: a group this shape's state fits
+static int check_push(const tops_gla_shape& s, const tops_gla_p2p_args* x) {
+  TOPS_CHECK_ARG(x != nullptr, "span_begin_p2p: p2p args are required");
+  TOPS_CHECK_ARG(x->world > 0 && x->world <= p2p::MAX_WORLD && x->rank >= 0 && x->rank < x->world,
+                 "span_begin_p2p: bad rank / world (at most 64 ranks)");
+  TOPS_CHECK_ARG(x->regions && x->own_region, "span_begin_p2p: regions (device array) and own_region are required");
+  TOPS_CHECK_ARG(x->N == s.B && x->H == s.H && x->K == s.K && x->V == s.V,
+                 "span_begin_p2p: the p2p shape (N, H, K, V) must be the problem's (B, H, K, V)");
+  return TOPS_OK;
+}
+
+int tops_gla_chunk_fwd_span_begin_p2p(const tops_gla_chunk_fwd_args* a, float* decay, const tops_gla_p2p_args* x,
+                                      void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_fwd_span_begin_p2p: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc || (rc = check_push(a->s, x))) return rc;
+  TOPS_CHECK_ARG(a->q && a->k && a->v && decay, "chunk_fwd_span_begin_p2p: q, k, v and decay are required");
+  const p2p::PeerPush push{x->regions, x->own_region, x->rank, x->world, nullptr};
+  return tc::fwd_span_begin(a->s, a->q, a->k, a->v, a->g, a->saved, nullptr, decay, S(stream), &push);
+}
+
 int tops_gla_chunk_fwd_span_finish(const tops_gla_chunk_fwd_args* a, void* stream) {
   TOPS_CHECK_ARG(a != nullptr, "chunk_fwd_span_finish: args is NULL");
   int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
@@ -493,6 +515,16 @@ int tops_gla_chunk_bwd_span_begin(const tops_gla_chunk_bwd_args* a, float* local
   if (rc || (rc = check_bwd_span_ws(a))) return rc;
   TOPS_CHECK_ARG(a->do_ && local_dh0, "chunk_bwd_span_begin: do and local_dh0 are required");
   return tc::bwd_span_begin(a->s, a->do_, a->saved, a->workspace, local_dh0, S(stream));
+}
+
+int tops_gla_chunk_bwd_span_begin_p2p(const tops_gla_chunk_bwd_args* a, const float* decay, const tops_gla_p2p_args* x,
+                                      void* stream) {
+  TOPS_CHECK_ARG(a != nullptr, "chunk_bwd_span_begin_p2p: args is NULL");
+  int rc = check_span(&a->s, a->saved, a->saved_bytes, a->g);
+  if (rc || (rc = check_bwd_span_ws(a)) || (rc = check_push(a->s, x))) return rc;
+  TOPS_CHECK_ARG(a->do_ && decay, "chunk_bwd_span_begin_p2p: do and decay are required");
+  const p2p::PeerPush push{x->regions, x->own_region, x->rank, x->world, decay};
+  return tc::bwd_span_begin(a->s, a->do_, a->saved, a->workspace, nullptr, S(stream), &push);
 }
 
 int tops_gla_chunk_bwd_span_finish(const tops_gla_chunk_bwd_args* a, void* stream) {

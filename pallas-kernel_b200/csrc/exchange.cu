@@ -19,6 +19,7 @@
 #include <thread>
 
 #include "common.cuh"
+#include "p2p.cuh"
 #include "ptx.cuh"
 
 namespace tops {
@@ -99,46 +100,20 @@ __global__ void k_combine(int world, int rank, int backward, size_t ns, int V, c
 }
 
 // ---------------------------------------------------------------------------
-// Peer-memory exchange (one process per GPU, every rank's receive region mapped into every
-// process).  A region: a 4 KB control block -- flags[2][P2P_MAX_WORLD] (the epoch whose slot
-// rank j has written, per slot parity), the epoch of this rank's last exchange, a block
-// counter -- then slots[2][world][per] of fp32 packed (state | decay).  Exchange e writes
-// slot parity e & 1: rank r's slot of e + 2 is written only after every rank has finished
+// Peer-memory exchange (regions and flag protocol in p2p.cuh).  Exchange e writes slot
+// parity e & 1: rank r's slot of e + 2 is written only after every rank has finished
 // reading e (each rank's push of e + 1 follows its combine of e on its stream, and rank r
 // pushes e + 2 only after its combine of e + 1 saw every rank's push of e + 1).
 // ---------------------------------------------------------------------------
-constexpr size_t P2P_CTRL = 4096;
-constexpr int P2P_MAX_WORLD = 64;
-__device__ __forceinline__ uint32_t* p2p_flags(void* region) { return reinterpret_cast<uint32_t*>(region); }
-__device__ __forceinline__ uint32_t* p2p_epoch(void* region) {
-  return reinterpret_cast<uint32_t*>(static_cast<char*>(region) + 1024);
-}
-__device__ __forceinline__ uint32_t* p2p_done(void* region) {
-  return reinterpret_cast<uint32_t*>(static_cast<char*>(region) + 1028);
-}
-__device__ __forceinline__ float* p2p_slots(void* region) {
-  return reinterpret_cast<float*>(static_cast<char*>(region) + P2P_CTRL);
-}
-__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) { return *reinterpret_cast<const volatile uint32_t*>(p); }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // This rank's packed (state | decay) into its slot of every rank's region (plain stores
-// through the peer mappings, NVLink), then -- once every block's stores are fenced -- the
-// epoch into every rank's flag for this rank.  `vec`: per, ns and the pointers allow 16-byte
-// accesses.
+// through the peer mappings, NVLink), then the epoch flags (p2p::signal).  `vec`: per, ns and
+// the pointers allow 16-byte accesses.
 __global__ void k_p2p_push(int rank, int world, size_t ns, size_t nd, const float* __restrict__ s,
                            const float* __restrict__ d, void* const* __restrict__ regions, void* own, int vec) {
-  const uint32_t epoch = ld_volatile(p2p_epoch(own)) + 1u;
-  const uint32_t par = epoch & 1u;
+  const uint32_t epoch = p2p::next_epoch(own);
   const size_t per = ns + nd;
-  const size_t slot = ((size_t)par * world + rank) * per;
+  const size_t slot = p2p::slot_offset(epoch, world, rank, per);
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   if (vec) {
     const size_t per4 = per / 4, ns4 = ns / 4;
@@ -146,24 +121,15 @@ __global__ void k_p2p_push(int rank, int world, size_t ns, size_t nd, const floa
     const float4* d4 = reinterpret_cast<const float4*>(d);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < per4; i += stride) {
       const float4 x = i < ns4 ? s4[i] : d4[i - ns4];
-      for (int p = 0; p < world; ++p) reinterpret_cast<float4*>(p2p_slots(regions[p]) + slot)[i] = x;
+      for (int p = 0; p < world; ++p) reinterpret_cast<float4*>(p2p::slots(regions[p]) + slot)[i] = x;
     }
   } else {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += stride) {
       const float x = i < ns ? s[i] : d[i - ns];
-      for (int p = 0; p < world; ++p) p2p_slots(regions[p])[slot + i] = x;
+      for (int p = 0; p < world; ++p) p2p::slots(regions[p])[slot + i] = x;
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    if (atomicAdd(p2p_done(own), 1u) == gridDim.x - 1) {  // the last block: every block's stores are fenced
-      __threadfence_system();
-      for (int p = 0; p < world; ++p) st_release_sys(p2p_flags(regions[p]) + par * P2P_MAX_WORLD + rank, epoch);
-      *p2p_done(own) = 0u;
-      *p2p_epoch(own) = epoch;
-    }
-  }
+  p2p::signal(regions, own, world, rank, epoch);
 }
 
 // Wait (bounded: limit_ns, then DEVERR_PEER_TIMEOUT and no output) until every rank's slot of
@@ -173,14 +139,14 @@ __global__ void k_p2p_combine(int world, int rank, int backward, size_t ns, int 
                               const float* __restrict__ boundary, float* __restrict__ out, float* __restrict__ total,
                               uint64_t limit_ns) {
   __shared__ int ok;
-  const uint32_t epoch = ld_volatile(p2p_epoch(own));
+  const uint32_t epoch = p2p::ld_volatile(p2p::epoch_word(own));
   const uint32_t par = epoch & 1u;
   if (threadIdx.x == 0) {
     int good = 1;
-    const uint32_t* fl = p2p_flags(own) + par * P2P_MAX_WORLD;
+    const uint32_t* fl = p2p::flags(own) + par * p2p::MAX_WORLD;
     const uint64_t t0 = ptx::globaltimer_ns();
     for (int j = 0; j < world && good; ++j) {
-      while ((int32_t)(ld_acquire_sys(fl + j) - epoch) < 0) {
+      while ((int32_t)(p2p::ld_acquire_sys(fl + j) - epoch) < 0) {
         if (ptx::globaltimer_ns() - t0 > limit_ns) {
           ptx::record_error(ptx::DEVERR_PEER_TIMEOUT);
           good = 0;
@@ -192,7 +158,7 @@ __global__ void k_p2p_combine(int world, int rank, int backward, size_t ns, int 
   }
   __syncthreads();
   if (!ok) return;
-  combine_elems(world, rank, backward, ns, V, p2p_slots(own) + (size_t)par * world * (ns + ns / V), boundary, out,
+  combine_elems(world, rank, backward, ns, V, p2p::slots(own) + (size_t)par * world * (ns + ns / V), boundary, out,
                 total);
 }
 
@@ -323,13 +289,13 @@ TOPS_API int tops_gla_state_exchange(const tops_gla_exchange_args* a, void* stre
 
 
 TOPS_API size_t tops_gla_p2p_region_size(const tops_gla_p2p_args* a) {
-  if (!a || a->world <= 0 || a->world > P2P_MAX_WORLD || a->N <= 0 || a->H <= 0 || a->K <= 0 || a->V <= 0) return 0;
+  if (!a || a->world <= 0 || a->world > p2p::MAX_WORLD || a->N <= 0 || a->H <= 0 || a->K <= 0 || a->V <= 0) return 0;
   const size_t ns = (size_t)a->N * a->H * a->K * a->V, nd = (size_t)a->N * a->H * a->K;
-  return P2P_CTRL + 2 * (size_t)a->world * (ns + nd) * sizeof(float);
+  return p2p::CTRL + 2 * (size_t)a->world * (ns + nd) * sizeof(float);
 }
 
 TOPS_API int tops_gla_p2p_alloc(size_t bytes, void** region) {
-  TOPS_CHECK_ARG(region && bytes > P2P_CTRL, "p2p_alloc: a region of at least its control block is required");
+  TOPS_CHECK_ARG(region && bytes > p2p::CTRL, "p2p_alloc: a region of at least its control block is required");
   *region = nullptr;
   cudaError_t e = cudaMalloc(region, bytes);
   if (e == cudaSuccess) e = cudaMemset(*region, 0, bytes);
@@ -374,7 +340,7 @@ TOPS_API int tops_gla_ipc_close(void* region) {
 
 TOPS_API int tops_gla_p2p_exchange(const tops_gla_p2p_args* a, void* stream) {
   TOPS_CHECK_ARG(a, "p2p_exchange: args are required");
-  TOPS_CHECK_ARG(a->world > 0 && a->world <= P2P_MAX_WORLD && a->rank >= 0 && a->rank < a->world,
+  TOPS_CHECK_ARG(a->world > 0 && a->world <= p2p::MAX_WORLD && a->rank >= 0 && a->rank < a->world,
                  "p2p_exchange: bad rank / world (at most 64 ranks)");
   TOPS_CHECK_ARG(a->N > 0 && a->H > 0 && a->K > 0 && a->V > 0, "p2p_exchange: bad shape");
   TOPS_CHECK_ARG(a->local_state && a->decay && a->out, "p2p_exchange: local_state, decay and out are required");
@@ -392,13 +358,23 @@ TOPS_API int tops_gla_p2p_exchange(const tops_gla_p2p_args* a, void* stream) {
                                         a->own_region, vec);
     TOPS_CUDA_LAUNCH_CHECK("p2p_exchange push");
   }
-  {
-    LaunchTimer lt(st, "exchange_p2p_combine");
-    const int cb = (int)((ns + 255) / 256 < 4096 ? (ns + 255) / 256 : 4096);
-    k_p2p_combine<<<cb, 256, 0, st>>>(a->world, a->rank, a->backward, ns, a->V, a->own_region, a->boundary, a->out,
-                                      a->backward ? nullptr : a->total, (uint64_t)a->timeout_ms * 1000000ull);
-    TOPS_CUDA_LAUNCH_CHECK("p2p_exchange combine");
-  }
+  return tops_gla_p2p_combine(a, stream);
+}
+
+TOPS_API int tops_gla_p2p_combine(const tops_gla_p2p_args* a, void* stream) {
+  TOPS_CHECK_ARG(a, "p2p_combine: args are required");
+  TOPS_CHECK_ARG(a->world > 0 && a->world <= p2p::MAX_WORLD && a->rank >= 0 && a->rank < a->world,
+                 "p2p_combine: bad rank / world (at most 64 ranks)");
+  TOPS_CHECK_ARG(a->N > 0 && a->H > 0 && a->K > 0 && a->V > 0, "p2p_combine: bad shape");
+  TOPS_CHECK_ARG(a->out && a->own_region, "p2p_combine: out and own_region are required");
+  TOPS_CHECK_ARG(a->timeout_ms > 0, "p2p_combine: timeout_ms must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t ns = (size_t)a->N * a->H * a->K * a->V;
+  LaunchTimer lt(st, "exchange_p2p_combine");
+  const int cb = (int)((ns + 255) / 256 < 4096 ? (ns + 255) / 256 : 4096);
+  k_p2p_combine<<<cb, 256, 0, st>>>(a->world, a->rank, a->backward, ns, a->V, a->own_region, a->boundary, a->out,
+                                    a->backward ? nullptr : a->total, (uint64_t)a->timeout_ms * 1000000ull);
+  TOPS_CUDA_LAUNCH_CHECK("p2p_exchange combine");
   return TOPS_OK;
 }
 

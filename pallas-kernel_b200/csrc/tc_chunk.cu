@@ -39,6 +39,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "p2p.cuh"
 #include "ptx.cuh"
 
 namespace tops {
@@ -617,23 +618,46 @@ __global__ void k_span_prefix(int S, int B, int H, int K, int V, const float* __
 // A rank's whole span from the per-span results of a zero-state pass (E, P): its final state
 // from a zero state, out = fold over spans (out <- P_s out + E_s, from 0), and optionally its
 // total decay dout = prod_s P_s (per state row).  One thread per 4 consecutive state columns.
+// The span's own final state from a zero state S = fold over the in-GPU spans of (P, E), and
+// (dout) the product of their decays.  PUSH: S, and the decay (push.decay_in if given, else
+// the product), also go straight into this rank's slot of every rank's peer-memory region,
+// followed by the exchange's epoch flags (p2p.cuh) -- the state computation and its transfer
+// to the other GPUs in one kernel.  `out` may then be null.
+template <bool PUSH>
 __global__ void k_span_total(int S, int B, int H, int K, int V, const float* __restrict__ P,
-                             const float* __restrict__ E, float* __restrict__ out, float* __restrict__ dout) {
+                             const float* __restrict__ E, float* __restrict__ out, float* __restrict__ dout,
+                             p2p::PeerPush push) {
   const size_t n4 = (size_t)B * H * K * V / 4;
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= n4) return;
   const size_t per = (size_t)B * H * K * V, rows = (size_t)B * H * K;
-  const size_t row = idx * 4 / V;  // (b*H + h)*K + k
-  float4 cur = make_float4(0.f, 0.f, 0.f, 0.f);
-  float dp = 1.f;
-  for (int s = 0; s < S; ++s) {
-    const float d = P[s * rows + row];
-    const float4 x = reinterpret_cast<const float4*>(E + s * per)[idx];
-    cur = make_float4(fmaf(d, cur.x, x.x), fmaf(d, cur.y, x.y), fmaf(d, cur.z, x.z), fmaf(d, cur.w, x.w));
-    dp *= d;
+  uint32_t epoch = 0;
+  size_t slot = 0;
+  if constexpr (PUSH) {
+    epoch = p2p::next_epoch(push.own);
+    slot = p2p::slot_offset(epoch, push.world, push.rank, per + rows);
   }
-  reinterpret_cast<float4*>(out)[idx] = cur;
-  if (dout != nullptr && (idx * 4) % V == 0) dout[row] = dp;
+  if (idx < n4) {
+    const size_t row = idx * 4 / V;  // (b*H + h)*K + k
+    float4 cur = make_float4(0.f, 0.f, 0.f, 0.f);
+    float dp = 1.f;
+    for (int s = 0; s < S; ++s) {
+      const float d = P[s * rows + row];
+      const float4 x = reinterpret_cast<const float4*>(E + s * per)[idx];
+      cur = make_float4(fmaf(d, cur.x, x.x), fmaf(d, cur.y, x.y), fmaf(d, cur.z, x.z), fmaf(d, cur.w, x.w));
+      dp *= d;
+    }
+    if (out != nullptr) reinterpret_cast<float4*>(out)[idx] = cur;
+    const bool row_start = (idx * 4) % V == 0;
+    if (dout != nullptr && row_start) dout[row] = dp;
+    if constexpr (PUSH) {
+      for (int p = 0; p < push.world; ++p) reinterpret_cast<float4*>(p2p::slots(push.regions[p]) + slot)[idx] = cur;
+      if (row_start) {
+        const float dv = push.decay_in != nullptr ? push.decay_in[row] : dp;
+        for (int p = 0; p < push.world; ++p) p2p::slots(push.regions[p])[slot + per + row] = dv;
+      }
+    }
+  }
+  if constexpr (PUSH) p2p::signal(push.regions, push.own, push.world, push.rank, epoch);
 }
 
 // ===========================================================================
@@ -2165,16 +2189,23 @@ static Spans spans_of(const tops_gla_shape& s) { return spans_for(s, (s.T + BT -
 size_t span_saved_bytes(const tops_gla_shape& s) { return carve_saved(s, nullptr, nullptr, true, true); }
 
 static int span_total(const tops_gla_shape& s, Spans spn, const SpanBufs& sb, float* out, float* dout,
-                      cudaStream_t st) {
-  LaunchTimer lt(st, "tc_span_total");
+                      cudaStream_t st, const p2p::PeerPush* push = nullptr) {
   const size_t n4 = (size_t)s.B * s.H * s.K * s.V / 4;
-  k_span_total<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, sb.P, sb.E, out, dout);
-  TOPS_CUDA_LAUNCH_CHECK("tc_span_total");
+  const unsigned blocks = (unsigned)((n4 + 255) / 256);
+  if (push == nullptr) {
+    LaunchTimer lt(st, "tc_span_total");
+    k_span_total<false><<<blocks, 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, sb.P, sb.E, out, dout, p2p::PeerPush{});
+    TOPS_CUDA_LAUNCH_CHECK("tc_span_total");
+  } else {
+    LaunchTimer lt(st, "tc_span_total_push");
+    k_span_total<true><<<blocks, 256, 0, st>>>(spn.n, s.B, s.H, s.K, s.V, sb.P, sb.E, out, dout, *push);
+    TOPS_CUDA_LAUNCH_CHECK("tc_span_total_push");
+  }
   return TOPS_OK;
 }
 
 int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g, void* saved,
-                   float* local_state, float* decay, cudaStream_t st) {
+                   float* local_state, float* decay, cudaStream_t st, const p2p::PeerPush* push) {
   Saved sv;
   carve_saved(s, saved, &sv, true, true);
   PrepMaps pm;
@@ -2184,7 +2215,7 @@ int fwd_span_begin(const tops_gla_shape& s, const void* q, const void* k, const 
   int rc;
   if (sv.vb != nullptr && (rc = to_bf16(v, sv.vb, (size_t)s.B * s.T * s.H * s.V, st))) return rc;
   if ((rc = launch_prep(s, pm, sv, st)) || (rc = scan_spans_zero(s, sm, 0, sv.D, sv.sb, spn, st))) return rc;
-  return span_total(s, spn, sv.sb, local_state, decay, st);
+  return span_total(s, spn, sv.sb, local_state, decay, st, push);
 }
 
 int fwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,
@@ -2223,7 +2254,7 @@ static void carve_bwd_span(const tops_gla_shape& s, void* workspace, bf16** dhs,
 }
 
 int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, void* workspace, float* local_dh0,
-                   cudaStream_t st) {
+                   cudaStream_t st, const p2p::PeerPush* push) {
   Saved sv;
   carve_saved(s, const_cast<void*>(saved), &sv, true, true);
   bf16* dhs;
@@ -2239,7 +2270,7 @@ int bwd_span_begin(const tops_gla_shape& s, const void* dO, const void* saved, v
   if (!bwd_scan_maps(s, dO, sv, dhs, &sm)) return fail(TOPS_ERR_CUDA, "tc bwd span: cuTensorMapEncodeTiled failed");
   const Spans spn = spans_of(s);
   rc = scan_spans_zero(s, sm, 1, sv.D, sb, spn, st);
-  return rc ? rc : span_total(s, spn, sb, local_dh0, nullptr, st);
+  return rc ? rc : span_total(s, spn, sb, local_dh0, nullptr, st, push);
 }
 
 int bwd_span_finish(const tops_gla_shape& s, const void* q, const void* k, const void* v, const float* g,

@@ -143,6 +143,9 @@ SIGNATURES = {
     "tops_gla_ipc_open": (C.c_int, [VP, C.POINTER(VP)]),
     "tops_gla_ipc_close": (C.c_int, [VP]),
     "tops_gla_p2p_exchange": (C.c_int, [C.POINTER(P2PArgs), VP]),
+    "tops_gla_p2p_combine": (C.c_int, [C.POINTER(P2PArgs), VP]),
+    "tops_gla_chunk_fwd_span_begin_p2p": (C.c_int, [C.POINTER(ChunkFwdArgs), VP, C.POINTER(P2PArgs), VP]),
+    "tops_gla_chunk_bwd_span_begin_p2p": (C.c_int, [C.POINTER(ChunkBwdArgs), VP, C.POINTER(P2PArgs), VP]),
     "tops_gla_xla_chunk_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_chunk_bwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),
     "tops_gla_xla_recurrent_fwd": (None, [VP, VP, C.c_char_p, C.c_size_t, VP]),

@@ -215,7 +215,8 @@ class P2PStateExchange:
 
     _made = 0
 
-    def __init__(self, group=None, liveness_timeout: float | None = 30.0, timeout_s: float = 10.0):
+    def __init__(self, group=None, liveness_timeout: float | None = 30.0, timeout_s: float = 10.0,
+                 fused: bool = True):
         import socket
 
         from . import _C
@@ -230,6 +231,9 @@ class P2PStateExchange:
         if len({h for h, _ in where}) != 1 or len({u for _, u in where}) != self.world:
             raise ValueError("P2PStateExchange needs one process per GPU on one host (use NcclStateExchange)")
         self.regions = {}  # (N, H, K, V) -> (own region, [mapped peer regions], device table of all)
+        # chunk_gla_seq_parallel lets the span kernels that compute a rank's state push it into
+        # the regions themselves (tops_gla_chunk_{fwd,bwd}_span_begin_p2p + tops_gla_p2p_combine)
+        self.fused_push = bool(fused)
         self.watchdog = None
         P2PStateExchange._made += 1
         if liveness_timeout is not None and group is None:
@@ -339,6 +343,34 @@ class P2PStateExchange:
     def backward(self, L, D, dht=None):
         """-> the final-state gradient this rank's backward must use."""
         return self._run(True, L, D, dht, False)[0]
+
+    def push_args(self, shape):
+        """The ``_C.P2PArgs`` naming this group's regions for states of ``shape`` (N, H, K, V),
+        for a kernel that pushes this rank's state itself (the span-begin entry points);
+        checks the peers first."""
+        self.check_peers()
+        shape = tuple(int(x) for x in shape)
+        own, _, table = self._region(shape)
+        a = self._args(shape)
+        a.regions, a.own_region = self._C.ptr(table), own.value
+        return a
+
+    def combine(self, backward: bool, shape, boundary=None, want_total: bool = False, device=None):
+        """The receiving half after a fused push: wait for every rank's push of this epoch and
+        fold the prefix (forward: -> (incoming state, final state)) or suffix (backward: ->
+        (final-state gradient, None))."""
+        C = self._C
+        shape = tuple(int(x) for x in shape)
+        own, _, table = self._region(shape)
+        dev = self.device if device is None else device
+        boundary = None if boundary is None else boundary.float().contiguous()
+        out = torch.empty(shape, dtype=torch.float32, device=dev)
+        total = torch.empty(shape, dtype=torch.float32, device=dev) if want_total else None
+        a = self._args(shape, backward)
+        a.boundary, a.out, a.total = C.ptr(boundary), C.ptr(out), C.ptr(total)
+        a.regions, a.own_region = C.ptr(table), own.value
+        C.call("tops_gla_p2p_combine", a, C.stream_of(out))
+        return out, total
 
     def close(self):
         """Unmap and free the regions (collective: no rank frees its region while another may
@@ -486,6 +518,15 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
 
         p = _core.make_plan(q, v.shape[-1], chunk_size, None, scale)
         ctx.plan, ctx.group, ctx.has_h0, ctx.exchange = p, group, h0 is not None, exchange
+        if _core.span_saved_size(p, g) > 0 and getattr(exchange, "fused_push", False):
+            # tensor-core path, state pushed to the peers by the kernel that computes it
+            shape = (p.N, p.H, p.K, p.V)
+            D, blk = _core.fwd_span_begin_p2p(p, q, k, v, g, exchange.push_args(shape))
+            H_in, ht = exchange.combine(False, shape, h0, True, q.device)
+            o = _core.fwd_span_finish(p, q, k, v, g, H_in, blk)[0]
+            ctx.save_for_backward(q, k, v, g, H_in, D)
+            ctx.phased, ctx.fwd_saved = True, blk
+            return o, ht
         if _core.span_saved_size(p, g) > 0:
             # tensor-core path: two phases, nothing computed twice
             blk = {}
@@ -527,6 +568,12 @@ class _SeqParallelChunkGLA(torch.autograd.Function):
         want = ctx.has_h0 and rank == 0
         do = do.contiguous().to(q.dtype)
         dht = None if dht is None else dht.float()
+        if ctx.phased and getattr(ctx.exchange, "fused_push", False):
+            shape = (p.N, p.H, p.K, p.V)
+            ws = _core.bwd_span_begin_p2p(p, q, k, v, g, do, sv, D, ctx.exchange.push_args(shape))
+            G = ctx.exchange.combine(True, shape, dht, False, q.device)[0]
+            dq, dk, dv, dg, dh0 = _core.bwd_span_finish(p, q, k, v, g, do, G, sv, ws, want_dh0=want)
+            return dq, dk, dv, dg, dh0, None, None, None, None
         if ctx.phased:
             ws = {}
 

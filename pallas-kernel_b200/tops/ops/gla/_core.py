@@ -195,6 +195,19 @@ def fwd_span_begin(p: Plan, q, k, v, g):
     return S, D, blk
 
 
+def fwd_span_begin_p2p(p: Plan, q, k, v, g, x):
+    """Phase 1 with the state exchange's push fused into the kernel that computes the span's
+    state (``x``: a ``_C.P2PArgs`` naming the group's peer regions) -> (decay [N,H,K], saved
+    block).  The state itself goes only to the regions."""
+    dev = q.device
+    blk = torch.empty(span_saved_size(p, g), dtype=torch.uint8, device=dev)
+    D = torch.empty(p.N, p.H, p.K, dtype=torch.float32, device=dev)
+    a = _C.ChunkFwdArgs(p.shape(), _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(g), None, None, None,
+                        None, None, None, None, 0, _C.ptr(blk), blk.numel())
+    _C.call("tops_gla_chunk_fwd_span_begin_p2p", a, _C.ptr(D), x, _C.stream_of(q))
+    return D, blk
+
+
 def fwd_span_finish(p: Plan, q, k, v, g, h_in, blk, want_ht: bool = False):
     """Phase 2: the span's output from its incoming state ``h_in`` -> (o, ht|None)."""
     dev = q.device
@@ -222,6 +235,17 @@ def bwd_span_begin(p: Plan, q, k, v, g, do, blk):
     L = torch.empty(p.N, p.H, p.K, p.V, dtype=torch.float32, device=q.device)
     _C.call("tops_gla_chunk_bwd_span_begin", a, _C.ptr(L), _C.stream_of(q))
     return L, ws
+
+
+def bwd_span_begin_p2p(p: Plan, q, k, v, g, do, blk, D, x):
+    """Phase 1 of the backward with the exchange's push fused in: the span's local dh0 and
+    the forward's decay ``D`` go straight to the peer regions named by ``x`` -> workspace."""
+    a = _span_bwd_args(p, q, k, v, g, do, None, blk)
+    ws = torch.empty(max(int(_C.lib().tops_gla_chunk_bwd_span_workspace_size(a)), 1), dtype=torch.uint8,
+                     device=q.device)
+    a.workspace, a.workspace_bytes = _C.ptr(ws), ws.numel()
+    _C.call("tops_gla_chunk_bwd_span_begin_p2p", a, _C.ptr(D.contiguous()), x, _C.stream_of(q))
+    return ws
 
 
 def bwd_span_finish(p: Plan, q, k, v, g, do, dht_in, blk, ws, want_dh0: bool = False):

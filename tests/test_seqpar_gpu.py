@@ -80,13 +80,17 @@ def _worker(rank, world, port, out, use_exchange=False):
         exs.append(TD.P2PStateExchange())
     res = step(exs[0] if exs else None)
     if use_exchange == "p2p":
-        # the peer route equals the NCCL route bit for bit (the same combine arithmetic); a
-        # step's forward and backward exchanges use the two slot parities, and the second peer
-        # step reuses both slots
+        # the peer route -- the state pushed by the span kernel that computes it (the default)
+        # or by a separate push kernel (fused=False) -- equals the NCCL route bit for bit (the
+        # same fold and combine arithmetic); a step's forward and backward exchanges use the two
+        # slot parities, and the second fused step reuses both slots
         exs.append(TD.NcclStateExchange())
         ref = step(exs[1])
         again = step(exs[0])
-        res["same_as_nccl"] = all(torch.equal(res[nm], ref[nm]) and torch.equal(again[nm], ref[nm]) for nm in ref)
+        exs.append(TD.P2PStateExchange(fused=False))
+        unfused = step(exs[2])
+        res["same_as_nccl"] = all(torch.equal(res[nm], ref[nm]) and torch.equal(again[nm], ref[nm]) and
+                                  torch.equal(unfused[nm], ref[nm]) for nm in ref)
     out[rank] = res
     torch.cuda.synchronize()
     for ex in exs:
